@@ -1,0 +1,191 @@
+// Thin PyTorch extension over the focal_b200 C ABI; the replacement for the
+// reference's pybind11 binding (csrc/bindings.cpp:4-16) and its tensor-level
+// launcher (csrc/w4a16_gemv.cu:119-235).
+//
+// It keeps the reference's contract at the tensor level: inputs are CUDA,
+// contiguous and of the exact dtype; the output is allocated here with
+// torch::empty on x's device; work is queued on PyTorch's current stream under
+// a device guard; failures raise RuntimeError with the reference's messages.
+// All arithmetic happens in libfocal_b200.so behind include/focal_b200.h.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cmath>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "focal_b200.h"
+
+namespace {
+
+void check_tensor(const torch::Tensor& t, const char* name, c10::ScalarType dtype) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  TORCH_CHECK(t.scalar_type() == dtype, name, " has wrong dtype");
+}
+
+void raise_on(int rc) {
+  if (rc != FOCAL_OK) TORCH_CHECK(false, focal_last_error());
+}
+
+cudaStream_t current_stream() {
+  return reinterpret_cast<cudaStream_t>(at::cuda::getCurrentCUDAStream().stream());
+}
+
+// Validation in the reference's order and wording (csrc/w4a16_gemv.cu:157-177).
+void check_w4a16(const torch::Tensor& x, const torch::Tensor& wq, const torch::Tensor& scales,
+                 const torch::Tensor& zeros) {
+  check_tensor(x, "x", at::kBFloat16);
+  check_tensor(wq, "wq", at::kInt);
+  check_tensor(scales, "scales", at::kHalf);
+  check_tensor(zeros, "zeros", at::kHalf);
+  TORCH_CHECK(x.dim() == 2, "x must have shape [M, K]");
+  TORCH_CHECK(wq.dim() == 2, "wq must have shape [N, K / 8]");
+  TORCH_CHECK(scales.dim() == 2, "scales must have shape [N, K / 128]");
+  TORCH_CHECK(zeros.dim() == 2, "zeros must have shape [N, K / 128]");
+  TORCH_CHECK(wq.device() == x.device(), "wq must be on the same device as x");
+  TORCH_CHECK(scales.device() == x.device(), "scales must be on the same device as x");
+  TORCH_CHECK(zeros.device() == x.device(), "zeros must be on the same device as x");
+  const int64_t M = x.size(0), K = x.size(1), N = wq.size(0);
+  TORCH_CHECK(M <= INT32_MAX && K <= INT32_MAX && N <= INT32_MAX, "unsupported K/N");
+  raise_on(focal_w4a16_check_shape((int)M, (int)K, (int)N));
+  TORCH_CHECK(wq.size(1) == K / 8, "wq must have shape [N, K / 8]");
+  TORCH_CHECK(scales.size(0) == N && scales.size(1) == K / 128,
+              "scales must have shape [N, K / 128]");
+  TORCH_CHECK(zeros.size(0) == N && zeros.size(1) == K / 128,
+              "zeros must have shape [N, K / 128]");
+}
+
+torch::Tensor w4a16_linear(torch::Tensor x, torch::Tensor wq, torch::Tensor scales,
+                           torch::Tensor zeros) {
+  check_w4a16(x, wq, scales, zeros);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int M = (int)x.size(0), K = (int)x.size(1), N = (int)wq.size(0);
+  auto y = torch::empty({M, N}, x.options());
+  raise_on(focal_w4a16_gemv(x.data_ptr(), wq.data_ptr<int32_t>(), scales.data_ptr(),
+                            zeros.data_ptr(), y.data_ptr(), M, K, N, current_stream()));
+  return y;
+}
+
+torch::Tensor w4a16_linear_f32(torch::Tensor x, torch::Tensor wq, torch::Tensor scales,
+                               torch::Tensor zeros) {
+  check_w4a16(x, wq, scales, zeros);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int M = (int)x.size(0), K = (int)x.size(1), N = (int)wq.size(0);
+  auto y = torch::empty({M, N}, x.options().dtype(torch::kFloat32));
+  raise_on(focal_w4a16_gemv_f32(x.data_ptr(), wq.data_ptr<int32_t>(), scales.data_ptr(),
+                                zeros.data_ptr(), y.data_ptr<float>(), M, K, N,
+                                current_stream()));
+  return y;
+}
+
+torch::Tensor w4a16_gate_up_silu(torch::Tensor x, torch::Tensor wq_gate, torch::Tensor scales_gate,
+                                 torch::Tensor zeros_gate, torch::Tensor wq_up,
+                                 torch::Tensor scales_up, torch::Tensor zeros_up) {
+  check_w4a16(x, wq_gate, scales_gate, zeros_gate);
+  check_w4a16(x, wq_up, scales_up, zeros_up);
+  TORCH_CHECK(wq_up.sizes() == wq_gate.sizes(), "gate and up weights must have the same shape");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int M = (int)x.size(0), K = (int)x.size(1), N = (int)wq_gate.size(0);
+  auto h = torch::empty({M, N}, x.options());
+  raise_on(focal_w4a16_gate_up_silu(x.data_ptr(), wq_gate.data_ptr<int32_t>(),
+                                    scales_gate.data_ptr(), zeros_gate.data_ptr(),
+                                    wq_up.data_ptr<int32_t>(), scales_up.data_ptr(),
+                                    zeros_up.data_ptr(), h.data_ptr(), M, K, N, current_stream()));
+  return h;
+}
+
+torch::Tensor dequant(torch::Tensor wq, torch::Tensor scales, torch::Tensor zeros, int64_t K) {
+  check_tensor(wq, "wq", at::kInt);
+  check_tensor(scales, "scales", at::kHalf);
+  check_tensor(zeros, "zeros", at::kHalf);
+  TORCH_CHECK(wq.dim() == 2, "wq must have shape [N, K / 8]");
+  TORCH_CHECK(K % 128 == 0, "K must be divisible by 128");
+  const int64_t N = wq.size(0);
+  TORCH_CHECK(wq.size(1) * 8 == K, "wq shape does not match K");
+  TORCH_CHECK(scales.dim() == 2 && scales.size(0) == N && scales.size(1) == K / 128,
+              "scales must have shape [N, K / 128]");
+  TORCH_CHECK(zeros.dim() == 2 && zeros.size(0) == N && zeros.size(1) == K / 128,
+              "zeros must have shape [N, K / 128]");
+  const c10::cuda::CUDAGuard guard(wq.device());
+  auto w = torch::empty({N, K}, wq.options().dtype(torch::kFloat32));
+  raise_on(focal_w4a16_dequant(wq.data_ptr<int32_t>(), scales.data_ptr(), zeros.data_ptr(),
+                               w.data_ptr<float>(), (int)K, (int)N, current_stream()));
+  return w;
+}
+
+torch::Tensor pack_int4(torch::Tensor q) {
+  check_tensor(q, "w_q_uint8", at::kByte);
+  TORCH_CHECK(q.dim() == 2, "w_q_uint8 must have shape [N, K]");
+  const int64_t N = q.size(0), K = q.size(1);
+  TORCH_CHECK(K % 8 == 0, "K must be divisible by 8");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto wq = torch::empty({N, K / 8}, q.options().dtype(torch::kInt32));
+  raise_on(focal_pack_int4(q.data_ptr<uint8_t>(), wq.data_ptr<int32_t>(), (int)N, (int)K,
+                           current_stream()));
+  return wq;
+}
+
+// Split-KV workspace, one per (device, stream): its counters start at zero
+// (torch::zeros) and every successful call leaves them at zero, and calls on
+// one stream are ordered, so reuse is safe.
+std::mutex g_ws_mutex;
+std::map<std::pair<int, cudaStream_t>, torch::Tensor> g_ws;
+
+torch::Tensor workspace_for(const torch::Device& dev, cudaStream_t stream, size_t bytes) {
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  auto key = std::make_pair((int)dev.index(), stream);
+  auto it = g_ws.find(key);
+  if (it == g_ws.end() || (size_t)it->second.numel() < bytes) {
+    auto t = torch::zeros({(int64_t)bytes}, torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+    g_ws[key] = t;
+    return t;
+  }
+  return it->second;
+}
+
+torch::Tensor gqa_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                                   c10::optional<double> scale) {
+  check_tensor(q, "q", at::kBFloat16);
+  check_tensor(k_cache, "k_cache", at::kBFloat16);
+  check_tensor(v_cache, "v_cache", at::kBFloat16);
+  TORCH_CHECK(q.dim() == 3, "q must have shape [B, Hq, D]");
+  TORCH_CHECK(k_cache.dim() == 4, "k_cache must have shape [B, Hkv, L, D]");
+  TORCH_CHECK(v_cache.sizes() == k_cache.sizes(), "v_cache must have the shape of k_cache");
+  TORCH_CHECK(k_cache.device() == q.device(), "k_cache must be on the same device as q");
+  TORCH_CHECK(v_cache.device() == q.device(), "v_cache must be on the same device as q");
+  const int64_t B = q.size(0), Hq = q.size(1), D = q.size(2);
+  const int64_t Hkv = k_cache.size(1), L = k_cache.size(2);
+  TORCH_CHECK(k_cache.size(0) == B && k_cache.size(3) == D, "k_cache must have shape [B, Hkv, L, D]");
+  TORCH_CHECK(B <= INT32_MAX && L <= INT32_MAX, "unsupported size");
+  const double sc = scale.has_value() ? *scale : 1.0 / std::sqrt((double)D);
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto o = torch::empty({B, Hq, D}, q.options());
+  const cudaStream_t stream = current_stream();
+  const size_t ws_bytes = focal_gqa_decode_workspace_size((int)B, (int)Hq, (int)Hkv, (int)L, (int)D);
+  void* ws = nullptr;
+  torch::Tensor ws_t;
+  if (ws_bytes > 0) {
+    ws_t = workspace_for(q.device(), stream, ws_bytes);
+    ws = ws_t.data_ptr();
+  }
+  raise_on(focal_gqa_decode_attn(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(),
+                                 (int)B, (int)Hq, (int)Hkv, (int)L, (int)D, (float)sc, ws, ws_bytes,
+                                 stream));
+  return o;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("w4a16_linear", &w4a16_linear, "W4A16 small-M linear (B200 sm_100a)");
+  m.def("w4a16_linear_f32", &w4a16_linear_f32, "W4A16 small-M linear, fp32 output");
+  m.def("w4a16_gate_up_silu", &w4a16_gate_up_silu, "fused gate/up projections with SiLU(gate)*up");
+  m.def("dequant", &dequant, "fp32 dequantized weights (bit-identical to dequant_ref)");
+  m.def("pack_int4", &pack_int4, "pack uint8 [N,K] nibbles into int32 [N,K/8]");
+  m.def("gqa_decode_attention", &gqa_decode_attention, "contiguous GQA decode attention",
+        pybind11::arg("q"), pybind11::arg("k_cache"), pybind11::arg("v_cache"),
+        pybind11::arg("scale") = pybind11::none());
+}

@@ -1,0 +1,119 @@
+/*
+ * focal_b200 — C ABI of the B200-native (sm_100a) decode hot paths.
+ *
+ * Plain pointers, sizes and a CUDA stream; no framework types.  Every entry
+ * point is asynchronous on `stream`, returns FOCAL_OK (0) or a focal_status
+ * code, and leaves a message for focal_last_error() on failure.  Pointers are
+ * device pointers unless stated otherwise.  Shape errors use the reference's
+ * exact messages ("unsupported M", "unsupported K/N", ...).
+ *
+ * Reference interfaces replaced (paths within the reference project):
+ *   csrc/bindings.cpp:4-16        pybind11 module exporting w4a16_linear
+ *   csrc/w4a16_gemv.cu:119-235    check_tensor / check_shape / launch_w4a16
+ *   focal_w4a16/__init__.py:38-91 pack_int4_weight / dequant_ref
+ */
+#ifndef FOCAL_B200_H_
+#define FOCAL_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same typedef as the CUDA runtime's (driver_types.h); a NULL stream is the
+ * legacy default stream. */
+typedef struct CUstream_st* cudaStream_t;
+
+typedef enum focal_status {
+  FOCAL_OK = 0,
+  FOCAL_ERR_INVALID_VALUE = 1, /* null/misaligned pointer, bad argument        */
+  FOCAL_ERR_UNSUPPORTED = 2,   /* shape outside the contract                   */
+  FOCAL_ERR_WORKSPACE = 3,     /* workspace missing or too small               */
+  FOCAL_ERR_CUDA = 4,          /* CUDA runtime / driver error at launch        */
+  FOCAL_ERR_DEVICE = 5         /* a kernel reported a device-side failure      */
+} focal_status;
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* focal_last_error(void);
+
+/* ABI version of this library (bumped on any signature change). */
+int focal_abi_version(void);
+
+/* ---------------------------------------------------------------- W4A16 ---
+ * y[M,N] = bf16( x[M,K] . dequant(wq)[N,K]^T ), fp32 accumulation.
+ *   x      bf16  [M, K]      row-major, 16-byte aligned
+ *   wq     int32 [N, K/8]    eight uint4 per word, value k at bits 4*(k%8)
+ *   scales fp16  [N, K/128]  4-byte aligned
+ *   zeros  fp16  [N, K/128]  4-byte aligned
+ *   dequant: w[n,k] = (float(q) - float(zeros[n,k/128])) * float(scales[n,k/128])
+ * Contract: 1 <= M <= 8; N % 64 == 0; K % 256 == 0; K = N = 11008 is rejected
+ * ("unsupported K/N") as in the reference; M*K bounded by the on-chip
+ * activation buffer (K <= 32768 at M = 8).
+ */
+
+/* Host-only shape check; FOCAL_OK or FOCAL_ERR_UNSUPPORTED with the
+ * reference's message.  Replaces check_shape, csrc/w4a16_gemv.cu:129-149. */
+int focal_w4a16_check_shape(int M, int K, int N);
+
+/* The linear layer.  Replaces launch_w4a16 / w4a16_gemv_kernel,
+ * csrc/w4a16_gemv.cu:33-116 and :152-223; y is written, never read. */
+int focal_w4a16_gemv(const void* x, const int32_t* wq, const void* scales, const void* zeros,
+                     void* y, int M, int K, int N, cudaStream_t stream);
+
+/* Same product with an fp32 output (no bf16 rounding): the partial sum of a
+ * K-sharded (row-parallel) projection before its all-reduce.  New entry point;
+ * the reference has no multi-GPU path. */
+int focal_w4a16_gemv_f32(const void* x, const int32_t* wq, const void* scales, const void* zeros,
+                         float* y, int M, int K, int N, cudaStream_t stream);
+
+/* Fused decode MLP front half: h = bf16( silu(x.Wg^T) * (x.Wu^T) ), with Wg and
+ * Wu two W4A16 weights of identical shape [N, K/8] (gate and up projections).
+ * The reference times these as separate projections
+ * (bench/bench_decode_bundle.py:19-27); this entry point is new. */
+int focal_w4a16_gate_up_silu(const void* x, const int32_t* wq_gate, const void* scales_gate,
+                             const void* zeros_gate, const int32_t* wq_up, const void* scales_up,
+                             const void* zeros_up, void* h, int M, int K, int N,
+                             cudaStream_t stream);
+
+/* fp32 [N, K] dequantized weights, bit-identical to dequant_ref
+ * (focal_w4a16/__init__.py:57-91); exposes the kernels' int4 unpacking. */
+int focal_w4a16_dequant(const int32_t* wq, const void* scales, const void* zeros, float* w,
+                        int K, int N, cudaStream_t stream);
+
+/* uint8 [N, K] (low nibble used) -> int32 [N, K/8]; replaces pack_int4_weight,
+ * focal_w4a16/__init__.py:38-54.  K % 8 == 0. */
+int focal_pack_int4(const uint8_t* q, int32_t* wq, int N, int K, cudaStream_t stream);
+
+/* ------------------------------------------------- GQA decode attention ---
+ * o[b,h,:] = softmax( q[b,h,:] . k[b,g,:,:]^T * scale ) . v[b,g,:,:],  g = h / (Hq/Hkv)
+ *   q bf16 [B, Hq, D]; k, v bf16 [B, Hkv, L, D] contiguous; o bf16 [B, Hq, D]
+ * fp32 scores, softmax and accumulation; split-KV with a log-sum-exp combine.
+ * Contract: D == 128; Hq % Hkv == 0; Hq / Hkv <= 16; L >= 1.
+ * New component: the reference contains no attention code.
+ *
+ * Workspace (device memory, ws_bytes >= focal_gqa_decode_workspace_size(...)):
+ * split partials plus one arrival counter per (b, kv head).  The counters must
+ * be zero before the first call on a workspace; every call that returns
+ * FOCAL_OK leaves them zero again.  Calls sharing a workspace must be ordered
+ * on one stream.
+ */
+size_t focal_gqa_decode_workspace_size(int B, int Hq, int Hkv, int L, int D);
+
+int focal_gqa_decode_attn(const void* q, const void* k, const void* v, void* o, int B, int Hq,
+                          int Hkv, int L, int D, float scale, void* workspace, size_t ws_bytes,
+                          cudaStream_t stream);
+
+/* ------------------------------------------------------------ diagnostics ---
+ * Device-side status word of the current device: 0 while every kernel's
+ * bounded waits have completed; a nonzero focal device status otherwise.
+ * Synchronous (reads device memory).  focal_reset_device_status clears it. */
+int focal_device_status(int* status_out);
+int focal_reset_device_status(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FOCAL_B200_H_ */

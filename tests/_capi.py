@@ -1,0 +1,79 @@
+"""Test helpers: call the C ABI (include/focal_b200.h) on torch device tensors,
+and move tensors between torch and the numpy oracle's bit-pattern format."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from focal_b200 import _lib
+
+
+def stream_ptr():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def to_dev_bf16(bits: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).to(device)
+
+
+def bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def to_dev(a: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def gemv(x, wq, scales, zeros, out_dtype=torch.bfloat16):
+    M, K = x.shape
+    N = wq.shape[0]
+    y = torch.empty((M, N), dtype=out_dtype, device=x.device)
+    name = "focal_w4a16_gemv" if out_dtype == torch.bfloat16 else "focal_w4a16_gemv_f32"
+    _lib.call(name, ptr(x), ptr(wq), ptr(scales), ptr(zeros), ptr(y), M, K, N, stream_ptr())
+    return y
+
+
+def gate_up_silu(x, gate, up):
+    M, K = x.shape
+    N = gate[0].shape[0]
+    h = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    _lib.call("focal_w4a16_gate_up_silu", ptr(x), *map(ptr, gate), *map(ptr, up), ptr(h), M, K, N,
+              stream_ptr())
+    return h
+
+
+def dequant(wq, scales, zeros, K):
+    N = wq.shape[0]
+    w = torch.empty((N, K), dtype=torch.float32, device=wq.device)
+    _lib.call("focal_w4a16_dequant", ptr(wq), ptr(scales), ptr(zeros), ptr(w), K, N, stream_ptr())
+    return w
+
+
+def pack(q):
+    N, K = q.shape
+    wq = torch.empty((N, K // 8), dtype=torch.int32, device=q.device)
+    _lib.call("focal_pack_int4", ptr(q), ptr(wq), N, K, stream_ptr())
+    return wq
+
+
+def attention_workspace(B, Hq, Hkv, L, D, device):
+    n = _lib.lib().focal_gqa_decode_workspace_size(B, Hq, Hkv, L, D)
+    return torch.zeros(max(int(n), 256), dtype=torch.uint8, device=device), int(n)
+
+
+def attention(q, k, v, scale=None, ws=None):
+    B, Hq, D = q.shape
+    Hkv, L = k.shape[1], k.shape[2]
+    if scale is None:
+        scale = 1.0 / np.sqrt(D)
+    if ws is None:
+        ws = attention_workspace(B, Hq, Hkv, L, D, q.device)
+    buf, n = ws
+    o = torch.empty_like(q)
+    _lib.call("focal_gqa_decode_attn", ptr(q), ptr(k), ptr(v), ptr(o), B, Hq, Hkv, L, D,
+              float(scale), ptr(buf), n, stream_ptr())
+    return o

@@ -1,0 +1,160 @@
+"""W4A16 parity on the GPU, called through the C ABI (include/focal_b200.h).
+
+Bars:
+* dequant and packing: bit-exact against the oracle / the reference's fixtures;
+* outputs: allclose with atol 2e-2, rtol 1e-2 against the fp32-accumulated
+  reference after its bf16 cast (the product's tolerance), and the reference's
+  own metric max|d| <= 0.25, max|d|/max(|ref|,1) <= 0.03
+  (tests/test_correctness.py:9-19 of the reference);
+* fp32 outputs: within 2e-5 of the exact (float64) sum, relative to the row norm.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import w4a16 as ow
+from tests import _capi as C
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-2, 1e-2
+
+CONTRACT_KN = [(4096, 4096), (4096, 8192), (4096, 11008), (8192, 4096), (8192, 8192),
+               (8192, 11008), (11008, 4096)]
+
+
+def assert_parity(y_dev, ref_bits, what=""):
+    y = C.bf16_bits(y_dev)
+    rep = ow.allclose_report(y, ref_bits, ATOL, RTOL)
+    assert rep["allclose"], (what, rep)
+    assert rep["max_abs"] <= 0.25 and rep["max_rel"] <= 0.03, (what, rep)
+    return rep
+
+
+def dev_case(x, wq, s, z, device):
+    return (C.to_dev_bf16(x, device), C.to_dev(wq, device), C.to_dev(s, device),
+            C.to_dev(z, device))
+
+
+# --------------------------------------------------------------- dequant/pack
+@pytest.mark.parametrize("name", ["baseline", "refstyle"])
+def test_dequant_bit_exact_vs_reference_fixture(cuda, golden_dir, name):
+    d = dict(np.load(golden_dir / f"dequant_{name}.npz"))
+    K = int(d["K"])
+    w = C.dequant(C.to_dev(d["wq"], cuda), C.to_dev(d["scales"], cuda), C.to_dev(d["zeros"], cuda), K)
+    assert np.array_equal(w.cpu().numpy().view(np.uint32), d["deq"].view(np.uint32))
+
+
+def test_dequant_bit_exact_contract_shape(cuda):
+    _, wq, s, z = ow.baseline_case(1, 4096, 4096, seed=77)
+    w = C.dequant(C.to_dev(wq, cuda), C.to_dev(s, cuda), C.to_dev(z, cuda), 4096)
+    ref = ow.dequant(wq, s, z, 4096)
+    assert np.array_equal(w.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+def test_pack_matches_reference_fixture(cuda, golden_dir):
+    d = dict(np.load(golden_dir / "pack.npz"))
+    for q, packed in ((d["q"], d["packed"]), (d["ka_q"], d["ka_packed"])):
+        got = C.pack(C.to_dev(q, cuda)).cpu().numpy()
+        assert np.array_equal(got, packed)
+
+
+# --------------------------------------------------------------------- GEMV
+@pytest.mark.parametrize("name", ["linear_k512_n128.npz", "linear_k1024_n192.npz"])
+def test_gemv_vs_reference_fixture(cuda, golden_dir, name):
+    d = dict(np.load(golden_dir / name))
+    wq, s, z = (C.to_dev(d[k], cuda) for k in ("wq", "scales", "zeros"))
+    for M in (1, 2, 4, 8):
+        y = C.gemv(C.to_dev_bf16(d[f"x{M}"], cuda), wq, s, z)
+        assert_parity(y, d[f"y{M}"], f"{name} M={M}")
+
+
+def test_gemv_refstyle_generator_fixture(cuda, golden_dir):
+    d = dict(np.load(golden_dir / "linear_refstyle_m4.npz"))
+    x, wq, s, z = dev_case(d["x"], d["wq"], d["scales"], d["zeros"], cuda)
+    assert_parity(C.gemv(x, wq, s, z), d["y"])
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 6, 7, 8])
+def test_gemv_every_m_small(cuda, M):
+    x, wq, s, z = ow.baseline_case(M, 768, 320, seed=100 + M)  # 3 stages, 5 row blocks
+    y = C.gemv(*dev_case(x, wq, s, z, cuda))
+    assert_parity(y, ow.linear(x, wq, s, z), f"M={M}")
+
+
+@pytest.mark.parametrize("K,N", CONTRACT_KN)
+def test_gemv_contract_shapes(cuda, K, N):
+    x8, wq, s, z = ow.baseline_case(8, K, N, seed=1234 + K + N)
+    ref = ow.linear(x8, wq, s, z)
+    dwq, ds, dz = (C.to_dev(a, cuda) for a in (wq, s, z))
+    for M in (1, 2, 4, 8):
+        y = C.gemv(C.to_dev_bf16(x8[:M], cuda), dwq, ds, dz)
+        assert_parity(y, ref[:M], f"M={M} K={K} N={N}")
+
+
+def test_gemv_f32_output_matches_exact_sum(cuda):
+    x, wq, s, z = ow.baseline_case(8, 4096, 4096, seed=5)
+    y = C.gemv(*dev_case(x, wq, s, z, cuda), out_dtype=torch.float32).cpu().numpy().astype(np.float64)
+    exact = ow.linear_f64(x, wq, s, z)
+    err = np.abs(y - exact).max(axis=1) / np.linalg.norm(exact, axis=1)
+    assert np.all(err < 2e-5), err
+
+
+def test_gemv_deterministic(cuda):
+    x, wq, s, z = dev_case(*ow.baseline_case(8, 8192, 4096, seed=9), cuda)
+    a = C.gemv(x, wq, s, z)
+    b = C.gemv(x, wq, s, z)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+@pytest.mark.parametrize("g", [1, 2, 4, 8])
+def test_tensor_parallel_shards(cuda, g):
+    """Shards of the 70B-shaped layer at M=8: column-parallel K=8192, N=28672/g
+    (bf16 out) and row-parallel K=28672/g, N=8192 (fp32 partial out)."""
+    x, wq, s, z = ow.baseline_case(8, 8192, 28672 // g, seed=40 + g)
+    y = C.gemv(*dev_case(x, wq, s, z, cuda))
+    assert_parity(y, ow.linear(x, wq, s, z), f"column g={g}")
+    x, wq, s, z = ow.baseline_case(8, 28672 // g, 8192, seed=50 + g)
+    y = C.gemv(*dev_case(x, wq, s, z, cuda), out_dtype=torch.float32).cpu().numpy().astype(np.float64)
+    exact = ow.linear_f64(x, wq, s, z)
+    err = np.abs(y - exact).max(axis=1) / np.linalg.norm(exact, axis=1)
+    assert np.all(err < 2e-5), (g, err)
+
+
+def silu_mul_oracle(g_bits, u_bits):
+    g = ow.bf16_to_f32(g_bits).astype(np.float32)
+    u = ow.bf16_to_f32(u_bits).astype(np.float32)
+    sg = ow.bf16_to_f32(ow.f32_to_bf16(g / (np.float32(1) + np.exp(-g))))
+    return ow.f32_to_bf16(sg * u)
+
+
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_gate_up_silu_fused(cuda, M):
+    K, N = 4096, 11008
+    x, wg, sg, zg = ow.baseline_case(M, K, N, seed=900 + M)
+    _, wu, su, zu = ow.baseline_case(1, K, N, seed=950 + M)
+    ref = silu_mul_oracle(ow.linear(x, wg, sg, zg), ow.linear(x, wu, su, zu))
+    dx = C.to_dev_bf16(x, cuda)
+    gate = tuple(C.to_dev(a, cuda) for a in (wg, sg, zg))
+    up = tuple(C.to_dev(a, cuda) for a in (wu, su, zu))
+    assert_parity(C.gate_up_silu(dx, gate, up), ref, f"M={M}")
+
+
+# ------------------------------------------------------------------- errors
+def test_capi_rejects_bad_shapes_and_pointers(cuda):
+    from focal_b200 import _lib
+
+    L = _lib.lib()
+    assert L.focal_w4a16_check_shape(1, 4096, 4096) == 0
+    for (M, K, N, msg) in [(0, 4096, 4096, "unsupported M"), (9, 4096, 4096, "unsupported M"),
+                           (1, 4096, 100, "unsupported N"), (1, 11008, 11008, "unsupported K/N"),
+                           (1, 4224, 4096, "unsupported K/N"), (8, 65536, 4096, "unsupported K/N")]:
+        assert L.focal_w4a16_check_shape(M, K, N) == _lib.FOCAL_ERR_UNSUPPORTED
+        assert _lib.last_error() == msg
+    x, wq, s, z = dev_case(*ow.baseline_case(1, 512, 64, seed=1), cuda)
+    y = torch.empty((1, 64), dtype=torch.bfloat16, device=cuda)
+    rc = L.focal_w4a16_gemv(x.data_ptr() + 2, wq.data_ptr(), s.data_ptr(), z.data_ptr(),
+                            y.data_ptr(), 1, 512, 64, C.stream_ptr())
+    assert rc == _lib.FOCAL_ERR_INVALID_VALUE and "aligned" in _lib.last_error()
+    status = __import__("ctypes").c_int(-1)
+    assert L.focal_device_status(status) == 0 and status.value == 0

@@ -1,0 +1,67 @@
+"""CPU-only checks of the native boundary: the C-ABI library loads without a
+GPU, exports every entry point include/focal_b200.h declares, and its
+host-only functions (shape contract, workspace sizing) behave."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from focal_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "focal_b200.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(focal_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    assert "focal_w4a16_gemv" in names and "focal_gqa_decode_attn" in names
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+    assert L.focal_abi_version() == 1
+
+
+@pytest.mark.parametrize("M,K,N,msg", [
+    (1, 4096, 4096, None), (8, 11008, 4096, None), (3, 8192, 28672, None), (8, 28672, 8192, None),
+    (0, 4096, 4096, "unsupported M"), (9, 4096, 4096, "unsupported M"),
+    (1, 4096, 4100, "unsupported N"), (1, 4096, 0, "unsupported N"),
+    (1, 11008, 11008, "unsupported K/N"), (1, 4224, 4096, "unsupported K/N"),
+    (1, 100, 4096, "unsupported K/N"), (8, 40960, 4096, "unsupported K/N"),
+    (4, 40960, 4096, None),
+])
+def test_shape_contract(M, K, N, msg):
+    rc = _lib.lib().focal_w4a16_check_shape(M, K, N)
+    if msg is None:
+        assert rc == _lib.FOCAL_OK
+    else:
+        assert rc == _lib.FOCAL_ERR_UNSUPPORTED and _lib.last_error() == msg
+
+
+def test_attention_workspace_sizing():
+    L = _lib.lib()
+    small = L.focal_gqa_decode_workspace_size(1, 32, 8, 512, 128)
+    big = L.focal_gqa_decode_workspace_size(8, 32, 8, 32768, 128)
+    assert 0 < small < big
+    assert L.focal_gqa_decode_workspace_size(1, 32, 8, 512, 64) == 0  # unsupported head dim
+    assert L.focal_gqa_decode_workspace_size(1, 30, 8, 512, 128) == 0  # Hq % Hkv != 0
+
+
+def test_status_codes_have_messages_without_gpu():
+    L = _lib.lib()
+    # argument errors are caught on the host before any CUDA call
+    rc = L.focal_w4a16_gemv(None, None, None, None, None, 1, 4096, 4096, None)
+    assert rc == _lib.FOCAL_ERR_INVALID_VALUE and "null" in _lib.last_error()
+    rc = L.focal_pack_int4(None, None, 4, 12, None)
+    assert rc == _lib.FOCAL_ERR_UNSUPPORTED
+    with pytest.raises(_lib.FocalError, match="unsupported M"):
+        _lib.call("focal_w4a16_check_shape", 16, 4096, 4096)
+    assert isinstance(ctypes.c_int(0).value, int)
