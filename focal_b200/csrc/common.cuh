@@ -48,12 +48,14 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
+  // The suspend-time hint lets the hardware park the warp until the phase
+  // completes (or ~0.1 ms pass) instead of spinning through issue slots.
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(100000u)
       : "memory");
   return ok != 0;
 }
@@ -66,7 +68,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
   const long long t0 = clock64();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 64; ++i) {
+    for (int i = 0; i < 16; ++i) {
       if (mbar_try_wait(bar, parity)) return true;
     }
     if (clock64() - t0 > kWaitLimitCycles) return false;
@@ -104,9 +106,54 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory, completing on `bar`
+// (addresses 16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// ---------------------------------------------------- programmatic launch
+// Let the next kernel in the stream start launching (it still waits for this
+// grid's completion in its own griddep_wait before touching our outputs).
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Wait until the previous kernel in the stream has completed and its memory
+// is visible (a no-op when this kernel was not launched programmatically).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Order this thread's generic-proxy shared-memory accesses (ld.shared,
+// ldmatrix) before later async-proxy writes (TMA / bulk copies) to the same
+// memory.  A ring slot read with ordinary loads must pass through this fence
+// before it is released for refilling by TMA.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ------------------------------------------------------------ cp.async (LDGSTS)
+// 16-byte copy global -> shared, bypassing L1 (.cg).
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
 __device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// Wait until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Arrive on `bar` once every cp.async this thread issued so far has landed.
@@ -116,6 +163,14 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
 }
 
 // ------------------------------------------------------------- shared loads
+// Loads through a generic pointer into shared memory: the compiler sees them
+// as memory reads (ordered by the "memory" clobbers of the mbarrier waits and
+// arrives) and is free to schedule them early.
+template <typename T>
+__device__ __forceinline__ T ld_smem(const uint8_t* smem_base, uint32_t offset) {
+  return *reinterpret_cast<const T*>(smem_base + offset);
+}
+
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
@@ -161,7 +216,7 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, u
 // D = A(16x16, row) * B(16x8, col) + C, bf16 inputs, fp32 accumulate.
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                                uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
       "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -208,6 +263,14 @@ __device__ __forceinline__ void named_barrier(int id, int nthreads) {
 // caller folds the +128 into the zero point; no subtraction is issued here.
 __device__ __forceinline__ uint32_t nib_pair_bf16(uint32_t word, int i) {
   return ((word >> (4 * i)) & 0x000F000Fu) | 0x43004300u;
+}
+
+// The same pair with the mask and the bf16 128.0 pattern held in registers, so
+// each pair costs exactly one LOP3 ((a & b) | c, truth table 0xEA) plus the shift.
+__device__ __forceinline__ uint32_t nib_pair_bf16(uint32_t word, int i, uint32_t mask, uint32_t magic) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(word >> (4 * i)), "r"(mask), "r"(magic));
+  return r;
 }
 
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }

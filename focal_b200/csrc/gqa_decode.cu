@@ -228,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mma_bf16_16816(oacc[j], pa[0], pa[1], pa[2], pa[3], b0, b1);
       mma_bf16_16816(oacc[j + 1], pa[0], pa[1], pa[2], pa[3], b2, b3);
     }
+    fence_proxy_async_smem();  // our ldmatrix reads of this slot precede its TMA refill
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar + 8 * slot);
   }

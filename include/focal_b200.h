@@ -48,25 +48,33 @@ int focal_abi_version(void);
  *   scales fp16  [N, K/128]  4-byte aligned
  *   zeros  fp16  [N, K/128]  4-byte aligned
  *   dequant: w[n,k] = (float(q) - float(zeros[n,k/128])) * float(scales[n,k/128])
- * Contract: 1 <= M <= 8; N % 64 == 0; K % 256 == 0; K = N = 11008 is rejected
- * ("unsupported K/N") as in the reference; M*K bounded by the on-chip
- * activation buffer (K <= 32768 at M = 8).
+ * Contract: 1 <= M <= 8; N % 64 == 0; 0 < K <= 2^24 with K % 256 == 0;
+ * K = N = 11008 is rejected ("unsupported K/N") as the reference does.
  */
 
 /* Host-only shape check; FOCAL_OK or FOCAL_ERR_UNSUPPORTED with the
  * reference's message.  Replaces check_shape, csrc/w4a16_gemv.cu:129-149. */
 int focal_w4a16_check_shape(int M, int K, int N);
 
+/* Bytes of device workspace the three linear entry points below need for
+ * (M, K): the activations rearranged once per call into the tensor cores'
+ * fragment order plus their per-group sums (about 2*M*K bytes); 0 if (M, K)
+ * is outside the contract.  The workspace needs 16-byte alignment, no
+ * initialisation, and may be reused by calls ordered on one stream. */
+size_t focal_w4a16_workspace_size(int M, int K);
+
 /* The linear layer.  Replaces launch_w4a16 / w4a16_gemv_kernel,
  * csrc/w4a16_gemv.cu:33-116 and :152-223; y is written, never read. */
 int focal_w4a16_gemv(const void* x, const int32_t* wq, const void* scales, const void* zeros,
-                     void* y, int M, int K, int N, cudaStream_t stream);
+                     void* y, int M, int K, int N, void* workspace, size_t ws_bytes,
+                     cudaStream_t stream);
 
 /* Same product with an fp32 output (no bf16 rounding): the partial sum of a
  * K-sharded (row-parallel) projection before its all-reduce.  New entry point;
  * the reference has no multi-GPU path. */
 int focal_w4a16_gemv_f32(const void* x, const int32_t* wq, const void* scales, const void* zeros,
-                         float* y, int M, int K, int N, cudaStream_t stream);
+                         float* y, int M, int K, int N, void* workspace, size_t ws_bytes,
+                         cudaStream_t stream);
 
 /* Fused decode MLP front half: h = bf16( silu(x.Wg^T) * (x.Wu^T) ), with Wg and
  * Wu two W4A16 weights of identical shape [N, K/8] (gate and up projections).
@@ -74,8 +82,8 @@ int focal_w4a16_gemv_f32(const void* x, const int32_t* wq, const void* scales, c
  * (bench/bench_decode_bundle.py:19-27); this entry point is new. */
 int focal_w4a16_gate_up_silu(const void* x, const int32_t* wq_gate, const void* scales_gate,
                              const void* zeros_gate, const int32_t* wq_up, const void* scales_up,
-                             const void* zeros_up, void* h, int M, int K, int N,
-                             cudaStream_t stream);
+                             const void* zeros_up, void* h, int M, int K, int N, void* workspace,
+                             size_t ws_bytes, cudaStream_t stream);
 
 /* fp32 [N, K] dequantized weights, bit-identical to dequant_ref
  * (focal_w4a16/__init__.py:57-91); exposes the kernels' int4 unpacking. */

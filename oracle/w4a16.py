@@ -62,12 +62,17 @@ def pack_int4(q: np.ndarray) -> np.ndarray:
 
 
 def unpack_int4(wq: np.ndarray) -> np.ndarray:
-    """int32 [N, K/8] -> uint8 [N, K]; focal_w4a16/__init__.py:85-88."""
-    w = np.asarray(wq, dtype=np.int32).view(np.uint32)
-    n, kw = w.shape
-    shifts = (np.arange(8, dtype=np.uint32) * 4).reshape(1, 1, 8)
-    q = (w.reshape(n, kw, 1) >> shifts) & 0xF
-    return q.reshape(n, kw * 8).astype(np.uint8)
+    """int32 [N, K/8] -> uint8 [N, K]; focal_w4a16/__init__.py:85-88.
+
+    Byte j of a little-endian word holds values 2j (low nibble) and 2j+1
+    (high nibble), which is the reference's ``(word >> 4i) & 0xF`` order.
+    """
+    b = np.ascontiguousarray(wq, dtype=np.int32).view(np.uint8)
+    n, nb = b.shape
+    q = np.empty((n, nb, 2), dtype=np.uint8)
+    np.bitwise_and(b, 0xF, out=q[:, :, 0])
+    np.right_shift(b, 4, out=q[:, :, 1])
+    return q.reshape(n, nb * 2)
 
 
 # ------------------------------------------------------------------- dequant
@@ -88,10 +93,10 @@ def dequant(wq: np.ndarray, scales: np.ndarray, zeros: np.ndarray, K: int) -> np
     zeros = np.asarray(zeros, dtype=np.float16)
     if scales.shape != (n, K // GROUP) or zeros.shape != (n, K // GROUP):
         raise ValueError("scales/zeros must have shape [N, K / 128]")
-    q = unpack_int4(wq).astype(np.float32)
-    s = np.repeat(scales.astype(np.float32), GROUP, axis=1)
-    z = np.repeat(zeros.astype(np.float32), GROUP, axis=1)
-    return (q - z) * s
+    w = unpack_int4(wq).astype(np.float32).reshape(n, K // GROUP, GROUP)
+    np.subtract(w, zeros.astype(np.float32)[:, :, None], out=w)   # q - z   (fp32)
+    np.multiply(w, scales.astype(np.float32)[:, :, None], out=w)  # * s     (fp32)
+    return w.reshape(n, K)
 
 
 # -------------------------------------------------------------------- linear
@@ -151,3 +156,36 @@ def allclose_report(y_bf16: np.ndarray, ref_bf16: np.ndarray, atol: float = 2e-2
         "max_abs": float(d.max()) if d.size else 0.0,
         "max_rel": float((d / np.maximum(np.abs(r), 1.0)).max()) if d.size else 0.0,
     }
+
+
+# ------------------------------------------------------- timed CPU baseline
+def linear_threaded(x_bf16: np.ndarray, wq: np.ndarray, scales: np.ndarray, zeros: np.ndarray,
+                    threads: int) -> np.ndarray:
+    """``linear`` with the N rows split over ``threads`` worker threads.
+
+    Each worker dequantises its row block (``dequant``) and multiplies it with
+    single-threaded BLAS; numpy releases the GIL in both, so the blocks run in
+    parallel.  Same arithmetic per element as ``linear`` (fp32 dequant, fp32
+    accumulation, bf16 rounding).  Used as the timed CPU restatement of the
+    reference's baseline_dequant_matmul.
+    """
+    from concurrent.futures import ThreadPoolExecutor
+
+    from threadpoolctl import threadpool_limits
+
+    x = bf16_to_f32(x_bf16)
+    K = x.shape[1]
+    N = wq.shape[0]
+    y = np.empty((x.shape[0], N), dtype=np.float32)
+    rows = 256  # row blocks small enough that each block's temporaries stay in cache
+    starts = range(0, N, rows)
+
+    def work(a):
+        b = min(N, a + rows)
+        w = dequant(wq[a:b], scales[a:b], zeros[a:b], K)
+        y[:, a:b] = x @ w.T
+
+    with threadpool_limits(limits=1, user_api="blas"):
+        with ThreadPoolExecutor(max_workers=max(1, threads)) as ex:
+            list(ex.map(work, starts))
+    return f32_to_bf16(y)

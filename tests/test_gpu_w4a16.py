@@ -23,11 +23,16 @@ CONTRACT_KN = [(4096, 4096), (4096, 8192), (4096, 11008), (8192, 4096), (8192, 8
                (8192, 11008), (11008, 4096)]
 
 
-def assert_parity(y_dev, ref_bits, what=""):
+def assert_parity(y_dev, ref_bits, what="", reference_metric=True):
+    """allclose(2e-2, 1e-2) always; the reference's max-abs/max-rel metric for
+    plain projection outputs (its 0.25 absolute bound assumes |y| of a few tens)."""
     y = C.bf16_bits(y_dev)
     rep = ow.allclose_report(y, ref_bits, ATOL, RTOL)
     assert rep["allclose"], (what, rep)
-    assert rep["max_abs"] <= 0.25 and rep["max_rel"] <= 0.03, (what, rep)
+    if reference_metric:
+        assert rep["max_abs"] <= 0.25 and rep["max_rel"] <= 0.03, (what, rep)
+    else:
+        assert rep["max_rel"] <= 0.03, (what, rep)
     return rep
 
 
@@ -107,6 +112,24 @@ def test_gemv_deterministic(cuda):
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
+@pytest.mark.parametrize("M,K,N", [(1, 8192, 8192), (8, 16384, 4096), (2, 28672, 8192)])
+def test_gemv_ring_wrap_repeated(cuda, M, K, N):
+    """Shapes whose CTAs cycle the shared-memory ring several times, called
+    repeatedly with fresh output and workspace buffers: every call must match
+    the oracle bit-for-bit-stably (guards the slot release / refill ordering)."""
+    x, wq, s, z = ow.baseline_case(M, K, N, seed=K + N + M)
+    ref = ow.linear(x, wq, s, z)
+    dx, dw, ds, dz = dev_case(x, wq, s, z, cuda)
+    first = None
+    for _ in range(12):
+        y = C.gemv(dx, dw, ds, dz)
+        bits = C.bf16_bits(y)
+        if first is None:
+            first = bits
+            assert_parity(y, ref, f"M={M} K={K} N={N}")
+        assert np.array_equal(bits, first)
+
+
 @pytest.mark.parametrize("g", [1, 2, 4, 8])
 def test_tensor_parallel_shards(cuda, g):
     """Shards of the 70B-shaped layer at M=8: column-parallel K=8192, N=28672/g
@@ -137,7 +160,8 @@ def test_gate_up_silu_fused(cuda, M):
     dx = C.to_dev_bf16(x, cuda)
     gate = tuple(C.to_dev(a, cuda) for a in (wg, sg, zg))
     up = tuple(C.to_dev(a, cuda) for a in (wu, su, zu))
-    assert_parity(C.gate_up_silu(dx, gate, up), ref, f"M={M}")
+    # h = silu(g) * u reaches |h| ~ 1e2, where one bf16 step is 0.5
+    assert_parity(C.gate_up_silu(dx, gate, up), ref, f"M={M}", reference_metric=False)
 
 
 # ------------------------------------------------------------------- errors
@@ -148,13 +172,17 @@ def test_capi_rejects_bad_shapes_and_pointers(cuda):
     assert L.focal_w4a16_check_shape(1, 4096, 4096) == 0
     for (M, K, N, msg) in [(0, 4096, 4096, "unsupported M"), (9, 4096, 4096, "unsupported M"),
                            (1, 4096, 100, "unsupported N"), (1, 11008, 11008, "unsupported K/N"),
-                           (1, 4224, 4096, "unsupported K/N"), (8, 65536, 4096, "unsupported K/N")]:
+                           (1, 4224, 4096, "unsupported K/N"), (8, 1 << 25, 64, "unsupported K/N")]:
         assert L.focal_w4a16_check_shape(M, K, N) == _lib.FOCAL_ERR_UNSUPPORTED
         assert _lib.last_error() == msg
     x, wq, s, z = dev_case(*ow.baseline_case(1, 512, 64, seed=1), cuda)
     y = torch.empty((1, 64), dtype=torch.bfloat16, device=cuda)
+    buf, n = C.w4a16_workspace(1, 512, cuda)
     rc = L.focal_w4a16_gemv(x.data_ptr() + 2, wq.data_ptr(), s.data_ptr(), z.data_ptr(),
-                            y.data_ptr(), 1, 512, 64, C.stream_ptr())
+                            y.data_ptr(), 1, 512, 64, buf.data_ptr(), n, C.stream_ptr())
     assert rc == _lib.FOCAL_ERR_INVALID_VALUE and "aligned" in _lib.last_error()
+    rc = L.focal_w4a16_gemv(x.data_ptr(), wq.data_ptr(), s.data_ptr(), z.data_ptr(),
+                            y.data_ptr(), 1, 512, 64, buf.data_ptr(), n - 16, C.stream_ptr())
+    assert rc == _lib.FOCAL_ERR_WORKSPACE
     status = __import__("ctypes").c_int(-1)
     assert L.focal_device_status(status) == 0 and status.value == 0

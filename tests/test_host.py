@@ -35,8 +35,7 @@ def test_library_exports_every_declared_symbol():
     (0, 4096, 4096, "unsupported M"), (9, 4096, 4096, "unsupported M"),
     (1, 4096, 4100, "unsupported N"), (1, 4096, 0, "unsupported N"),
     (1, 11008, 11008, "unsupported K/N"), (1, 4224, 4096, "unsupported K/N"),
-    (1, 100, 4096, "unsupported K/N"), (8, 40960, 4096, "unsupported K/N"),
-    (4, 40960, 4096, None),
+    (1, 100, 4096, "unsupported K/N"), (8, 40960, 4096, None), (1, 1 << 25, 64, "unsupported K/N"),
 ])
 def test_shape_contract(M, K, N, msg):
     rc = _lib.lib().focal_w4a16_check_shape(M, K, N)
@@ -44,6 +43,15 @@ def test_shape_contract(M, K, N, msg):
         assert rc == _lib.FOCAL_OK
     else:
         assert rc == _lib.FOCAL_ERR_UNSUPPORTED and _lib.last_error() == msg
+
+
+def test_w4a16_workspace_sizing():
+    L = _lib.lib()
+    # one record per 256 K values: M' x 512 B of fragments + the group sums
+    assert L.focal_w4a16_workspace_size(1, 4096) == 16 * (512 + 16)
+    assert L.focal_w4a16_workspace_size(8, 4096) == 16 * (8 * 512 + 64)
+    assert L.focal_w4a16_workspace_size(3, 4096) == 16 * (4 * 512 + 32)
+    assert L.focal_w4a16_workspace_size(9, 4096) == 0
 
 
 def test_attention_workspace_sizing():
@@ -58,7 +66,7 @@ def test_attention_workspace_sizing():
 def test_status_codes_have_messages_without_gpu():
     L = _lib.lib()
     # argument errors are caught on the host before any CUDA call
-    rc = L.focal_w4a16_gemv(None, None, None, None, None, 1, 4096, 4096, None)
+    rc = L.focal_w4a16_gemv(None, None, None, None, None, 1, 4096, 4096, None, 0, None)
     assert rc == _lib.FOCAL_ERR_INVALID_VALUE and "null" in _lib.last_error()
     rc = L.focal_pack_int4(None, None, 4, 12, None)
     assert rc == _lib.FOCAL_ERR_UNSUPPORTED
