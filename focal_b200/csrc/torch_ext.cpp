@@ -37,8 +37,8 @@ cudaStream_t current_stream() {
 
 // Per-call W4A16 workspace from PyTorch's caching allocator (stream-ordered,
 // so a block freed after this call is only reused by later work on the stream).
-torch::Tensor w4a16_workspace(const torch::Tensor& x) {
-  const size_t n = focal_w4a16_workspace_size((int)x.size(0), (int)x.size(1));
+torch::Tensor w4a16_workspace(const torch::Tensor& x, int64_t N) {
+  const size_t n = focal_w4a16_workspace_size((int)x.size(0), (int)x.size(1), (int)N);
   return torch::empty({(int64_t)std::max<size_t>(n, 16)}, x.options().dtype(torch::kUInt8));
 }
 
@@ -72,7 +72,7 @@ torch::Tensor w4a16_linear(torch::Tensor x, torch::Tensor wq, torch::Tensor scal
   const c10::cuda::CUDAGuard guard(x.device());
   const int M = (int)x.size(0), K = (int)x.size(1), N = (int)wq.size(0);
   auto y = torch::empty({M, N}, x.options());
-  auto ws = w4a16_workspace(x);
+  auto ws = w4a16_workspace(x, N);
   raise_on(focal_w4a16_gemv(x.data_ptr(), wq.data_ptr<int32_t>(), scales.data_ptr(),
                             zeros.data_ptr(), y.data_ptr(), M, K, N, ws.data_ptr(), ws.numel(),
                             current_stream()));
@@ -85,7 +85,7 @@ torch::Tensor w4a16_linear_f32(torch::Tensor x, torch::Tensor wq, torch::Tensor 
   const c10::cuda::CUDAGuard guard(x.device());
   const int M = (int)x.size(0), K = (int)x.size(1), N = (int)wq.size(0);
   auto y = torch::empty({M, N}, x.options().dtype(torch::kFloat32));
-  auto ws = w4a16_workspace(x);
+  auto ws = w4a16_workspace(x, N);
   raise_on(focal_w4a16_gemv_f32(x.data_ptr(), wq.data_ptr<int32_t>(), scales.data_ptr(),
                                 zeros.data_ptr(), y.data_ptr<float>(), M, K, N, ws.data_ptr(),
                                 ws.numel(), current_stream()));
@@ -101,7 +101,7 @@ torch::Tensor w4a16_gate_up_silu(torch::Tensor x, torch::Tensor wq_gate, torch::
   const c10::cuda::CUDAGuard guard(x.device());
   const int M = (int)x.size(0), K = (int)x.size(1), N = (int)wq_gate.size(0);
   auto h = torch::empty({M, N}, x.options());
-  auto ws = w4a16_workspace(x);
+  auto ws = w4a16_workspace(x, N);
   raise_on(focal_w4a16_gate_up_silu(x.data_ptr(), wq_gate.data_ptr<int32_t>(),
                                     scales_gate.data_ptr(), zeros_gate.data_ptr(),
                                     wq_up.data_ptr<int32_t>(), scales_up.data_ptr(),

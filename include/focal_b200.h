@@ -57,11 +57,14 @@ int focal_abi_version(void);
 int focal_w4a16_check_shape(int M, int K, int N);
 
 /* Bytes of device workspace the three linear entry points below need for
- * (M, K): the activations rearranged once per call into the tensor cores'
- * fragment order plus their per-group sums (about 2*M*K bytes); 0 if (M, K)
- * is outside the contract.  The workspace needs 16-byte alignment, no
- * initialisation, and may be reused by calls ordered on one stream. */
-size_t focal_w4a16_workspace_size(int M, int K);
+ * (M, K, N) on the current device: the activations rearranged once per call
+ * into the tensor cores' fragment order with their per-group sums (about
+ * 2*M*K bytes), one arrival counter per 64 output rows, and the partial sums
+ * of row blocks that several CTAs share.  0 if the shape is outside the
+ * contract.  The workspace needs 256-byte alignment and no initialisation
+ * (each call clears what it uses); calls that share one must be ordered on a
+ * stream. */
+size_t focal_w4a16_workspace_size(int M, int K, int N);
 
 /* The linear layer.  Replaces launch_w4a16 / w4a16_gemv_kernel,
  * csrc/w4a16_gemv.cu:33-116 and :152-223; y is written, never read. */

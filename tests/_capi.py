@@ -28,16 +28,16 @@ def to_dev(a: np.ndarray, device) -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(a)).to(device)
 
 
-def w4a16_workspace(M, K, device):
-    n = int(_lib.lib().focal_w4a16_workspace_size(M, K))
-    return torch.empty(max(n, 16), dtype=torch.uint8, device=device), n
+def w4a16_workspace(M, K, N, device):
+    n = int(_lib.lib().focal_w4a16_workspace_size(M, K, N))
+    return torch.empty(max(n, 256), dtype=torch.uint8, device=device), n
 
 
 def gemv(x, wq, scales, zeros, out_dtype=torch.bfloat16, ws=None):
     M, K = x.shape
     N = wq.shape[0]
     y = torch.empty((M, N), dtype=out_dtype, device=x.device)
-    buf, n = ws if ws is not None else w4a16_workspace(M, K, x.device)
+    buf, n = ws if ws is not None else w4a16_workspace(M, K, N, x.device)
     name = "focal_w4a16_gemv" if out_dtype == torch.bfloat16 else "focal_w4a16_gemv_f32"
     _lib.call(name, ptr(x), ptr(wq), ptr(scales), ptr(zeros), ptr(y), M, K, N, ptr(buf), n, stream_ptr())
     return y
@@ -47,7 +47,7 @@ def gate_up_silu(x, gate, up):
     M, K = x.shape
     N = gate[0].shape[0]
     h = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
-    buf, n = w4a16_workspace(M, K, x.device)
+    buf, n = w4a16_workspace(M, K, N, x.device)
     _lib.call("focal_w4a16_gate_up_silu", ptr(x), *map(ptr, gate), *map(ptr, up), ptr(h), M, K, N,
               ptr(buf), n, stream_ptr())
     return h

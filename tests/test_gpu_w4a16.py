@@ -177,12 +177,12 @@ def test_capi_rejects_bad_shapes_and_pointers(cuda):
         assert _lib.last_error() == msg
     x, wq, s, z = dev_case(*ow.baseline_case(1, 512, 64, seed=1), cuda)
     y = torch.empty((1, 64), dtype=torch.bfloat16, device=cuda)
-    buf, n = C.w4a16_workspace(1, 512, cuda)
+    buf, n = C.w4a16_workspace(1, 512, 64, cuda)
     rc = L.focal_w4a16_gemv(x.data_ptr() + 2, wq.data_ptr(), s.data_ptr(), z.data_ptr(),
                             y.data_ptr(), 1, 512, 64, buf.data_ptr(), n, C.stream_ptr())
     assert rc == _lib.FOCAL_ERR_INVALID_VALUE and "aligned" in _lib.last_error()
     rc = L.focal_w4a16_gemv(x.data_ptr(), wq.data_ptr(), s.data_ptr(), z.data_ptr(),
-                            y.data_ptr(), 1, 512, 64, buf.data_ptr(), n - 16, C.stream_ptr())
+                            y.data_ptr(), 1, 512, 64, buf.data_ptr(), 1024, C.stream_ptr())
     assert rc == _lib.FOCAL_ERR_WORKSPACE
     status = __import__("ctypes").c_int(-1)
     assert L.focal_device_status(status) == 0 and status.value == 0

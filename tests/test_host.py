@@ -47,11 +47,15 @@ def test_shape_contract(M, K, N, msg):
 
 def test_w4a16_workspace_sizing():
     L = _lib.lib()
-    # one record per 256 K values: M' x 512 B of fragments + the group sums
-    assert L.focal_w4a16_workspace_size(1, 4096) == 16 * (512 + 16)
-    assert L.focal_w4a16_workspace_size(8, 4096) == 16 * (8 * 512 + 64)
-    assert L.focal_w4a16_workspace_size(3, 4096) == 16 * (4 * 512 + 32)
-    assert L.focal_w4a16_workspace_size(9, 4096) == 0
+    # activation records (one per 256 K values) come first; counters and
+    # split partials follow, so the size grows with M, K and N
+    a = L.focal_w4a16_workspace_size(1, 4096, 4096)
+    b = L.focal_w4a16_workspace_size(8, 4096, 4096)
+    c = L.focal_w4a16_workspace_size(8, 8192, 4096)
+    assert a >= 16 * (512 + 16) and b >= 16 * (8 * 512 + 64)
+    assert a < b < c
+    assert L.focal_w4a16_workspace_size(9, 4096, 4096) == 0
+    assert L.focal_w4a16_workspace_size(1, 4096, 100) == 0
 
 
 def test_attention_workspace_sizing():
