@@ -12,36 +12,36 @@
 //    one 16-byte-aligned record per 256 K values, into the caller's
 //    workspace; it also clears the row-block arrival counters.
 //
-// 2. w4a16_gemv, stream-K over units of (64 weight rows x 256 K values):
-//    the grid is exactly the number of CTAs that are resident at once, and
-//    CTA c takes the contiguous unit range [c*U/P, (c+1)*U/P) in row-block-
-//    major order, so every CTA streams the same number of bytes in a single
-//    wave.  Inside a CTA:
-//    * warp 8 (loader) fills a ring of 12 (gate/up: 8) slots.  Per unit: the packed
-//      weights as one 2-D TMA box of 64 rows x 128 bytes (128-byte swizzle),
-//      the unit's activation record as one bulk copy, and the fp16 scales and
-//      zeros: when K % 1024 == 0, one 2-D TMA box each of 64 rows x 8 groups
-//      per four units (a "quad", kept in its own 5-slot ring), otherwise the
+// 2. w4a16_gemv, stream-K over units of (64 weight rows x 256 K values), one
+//    resident CTA per SM made of four independent sub-pipelines.  The units
+//    are cut into P contiguous ranges (four per CTA), so every range streams
+//    the same number of bytes in a single wave.  Sub-pipeline p of a CTA owns
+//    one range, a ring of 3 slots (gate/up: 2), producer warp 8 + p and
+//    consumer warps 2p, 2p + 1; separate rings keep one slow box from
+//    stalling the other loads in flight, as a single in-order ring would.
+//    * the producer fills its ring.  Per unit: the packed weights as one 2-D
+//      TMA box of 64 rows x 128 bytes (128-byte swizzle), the unit's
+//      activation record as one bulk copy, and the fp16 scales and zeros:
+//      when K % 1024 == 0, one 2-D TMA box each of 64 rows x 8 groups per
+//      four units (a "quad", two quad slots per sub-pipeline), otherwise the
 //      unit's two groups per row with 4-byte cp.async.  All complete on the
-//      slot's mbarrier.  Weight and scale/zero boxes of the first ring-full
-//      start streaming before the previous kernel has finished (weights,
-//      scales and zeros must not be written by a kernel that triggers
-//      programmatic launch early); only the activation copies wait for it.
-//    * warps 0-7 (consumers), in four pairs: pair p takes the CTA's units
-//      i with i % 4 == p, so four units are consumed at once; the pair's two
-//      warps take one quantisation group each, over all 64 rows (four 16-row
-//      MMA tiles sharing one load of the group's activation fragments).  The
-//      slot's empty barrier waits for those two warps.  A packed word becomes bf16
-//      (128 + q) pairs with one shift and one LOP3 per pair, fed as the A
-//      fragment of mma.sync m16n8k16 (bf16 in, fp32 accumulate); the <= 8
-//      tokens are the n = 8 side.  Zero point and +128 factor out per group:
+//      slot's mbarrier.  The first ring-full of weight and scale/zero boxes
+//      is issued before the previous kernel has finished (weights, scales and
+//      zeros must not be written by a kernel that triggers programmatic
+//      launch early); only the activation copies wait for it.
+//    * the two consumer warps take one quantisation group each of every
+//      unit, over all 64 rows (four 16-row MMA tiles sharing one load of the
+//      group's activation fragments).  A packed word becomes bf16 (128 + q)
+//      pairs with one shift and one LOP3 per pair, fed as the A fragment of
+//      mma.sync m16n8k16 (bf16 in, fp32 accumulate); the <= 8 tokens are the
+//      n = 8 side.  Zero point and +128 factor out per group:
 //          sum_k x (q - z) s = s * (sum_k x (128 + q) - (z + 128) sum_k x)
 //      so the tensor core only sees exact small integers and x.
-//    * at the end of each row block's run of units the eight warps' shares are
-//      added in a fixed order, and the CTA either writes y
-//      (it had the whole row block) or stores its fp32 partial; the last CTA
-//      to arrive on the row block's counter adds all partials in CTA order
-//      (deterministic, no waiting) and writes y.
+//    * at the end of each row block's run in a range the two warps' shares
+//      are added (group 0 then group 1) and the sub-pipeline either writes y
+//      (its range held the whole row block) or stores its fp32 partial; the
+//      last range to arrive on the row block's counter adds all partials in
+//      range order (deterministic, no waiting) and writes y.
 //    No TMA multicast is used.
 #include <algorithm>
 #include <cmath>
@@ -58,31 +58,33 @@ constexpr int kStageK = 256;            // K values per unit / pipeline stage (t
 constexpr int kWordsPerStage = 32;      // int32 words per row per stage (128 B)
 constexpr int kRowTiles = 4;            // 16-row MMA tiles per unit
 constexpr int kRows = 16 * kRowTiles;   // weight rows per unit
-constexpr int kPairs = 4;               // consumer warp pairs; pair p takes every 4th unit
-constexpr int kConsumerWarps = 2 * kPairs;  // one warp per (pair, group of the unit)
+// The CTA runs kPairs independent sub-pipelines, each with its own unit range:
+// sub-pipeline p has producer warp 8 + p, a ring of ring_of(NW) slots and
+// consumer warps 2p, 2p + 1 (one per quantisation group of a unit).
+constexpr int kPairs = 4;
+constexpr int kConsumerWarps = 2 * kPairs;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
-constexpr int kLoaderWarp = kConsumerWarps;
-constexpr int kThreads = 32 * (kConsumerWarps + 1);
-// Ring slots: one resident CTA per SM (the 288-thread CTA is allocated as 12
-// warps, so its registers fill the SM), holding 96 KB (12 x 8 KB) or, for the
-// gate/up pair, 128 KB (8 x 16 KB) of weights in flight.
-__host__ __device__ constexpr int stages_of(int NW) { return NW == 1 ? 12 : 8; }
-constexpr int kMaxStages = 12;
-constexpr int kMaxCtasPerSm = 4;        // occupancy bound used to size the workspace
+constexpr int kThreads = 32 * (kConsumerWarps + kPairs);
+// One resident CTA per SM (12 warps at up to 160 registers): 12 x 8 KB (gate/up:
+// 8 x 16 KB) of weights in flight.
+__host__ __device__ constexpr int ring_of(int NW) { return NW == 1 ? 3 : 2; }
+constexpr int kMaxCtasPerSm = 4;        // bound on unit ranges per SM, used to size the workspace
 constexpr int kSumBatch = 8;            // partial sums loaded together by a finishing CTA
-constexpr int kMinUnitsPerCta = 4;      // below this, fewer CTAs beat more split overhead
-// Scale/zero quad slots when they arrive by TMA.  Pairs consume units out of
-// order, so a quad slot may only be refilled once every unit of the quad it
-// held is known consumed: the loader knows that of unit u once it has issued
-// unit u + stages.  With quads of four units (the first may have one) that
-// takes ceil((stages + 7) / 4) slots: 5 for 12 stages, 4 for 8.
-constexpr int kSzSlotsTma = 5;
-static_assert(4 * kSzSlotsTma >= kMaxStages + 7, "too few scale/zero quad slots for the ring depth");
+constexpr int kMinUnitsPerRange = 4;    // below this, fewer ranges beat more split overhead
+// Scale/zero quad slots per sub-pipeline when they arrive by TMA: the slot of
+// quad k is refilled for quad k + 2, whose first unit is issued only after the
+// unit ring_of(NW) places earlier (a unit of quad k + 1, or of quad k when k is
+// a one-unit quad) was consumed, and consumption within a sub-pipeline is in
+// order.
+constexpr int kSzQuadSlots = 2;
 constexpr int kSzQuadGroups = 8;        // groups per scale/zero TMA box (16 bytes of fp16)
-// bytes of scale/zero staging per weight matrix: the larger of the two modes
-constexpr uint32_t kSzSlotBytes =
-    (kSzSlotsTma * 2 * kRows * 16 > kMaxStages * 2 * kRows * 4) ? kSzSlotsTma * 2 * kRows * 16
-                                                                : kMaxStages * 2 * kRows * 4;
+// bytes of scale/zero staging per weight matrix: quads by TMA (16-byte rows) or
+// one unit per ring slot by cp.async (4-byte rows)
+constexpr uint32_t kSzTmaBytes = kPairs * kSzQuadSlots * 2 * kRows * 16;
+__host__ __device__ constexpr uint32_t sz_region_bytes(int NW) {
+  return kSzTmaBytes > (uint32_t)(kPairs * ring_of(NW) * 2 * kRows * 4) ? kSzTmaBytes
+                                                                       : kPairs * ring_of(NW) * 2 * kRows * 4;
+}
 
 enum Epi : int { kEpiBf16 = 0, kEpiF32 = 1, kEpiSiluMul = 2 };
 
@@ -185,26 +187,28 @@ struct Layout {
 __host__ __device__ constexpr uint32_t round_up(uint32_t a, uint32_t b) { return (a + b - 1) / b * b; }
 
 // Shared-memory carve-up, identical on host (sizing) and device (addressing).
+// Ring slot (p, j) is slot p * ring + j of each array.
 template <int MT, int NW>
 __host__ __device__ constexpr Layout make_layout() {
   Layout L{};
+  constexpr int slots = kPairs * ring_of(NW);
   uint32_t off = 0;
   L.w = off;  // [slot][mat][64 rows][128 B], 1024-aligned (swizzle atom)
-  off += stages_of(NW) * NW * kRows * 128;
+  off += slots * NW * kRows * 128;
   L.x = off;  // [slot] activation record
-  off += stages_of(NW) * rec_bytes(MT);
-  // scale / zero slots, [slot][mat][scale|zero][64 rows][row bytes]: either
-  // kSzSlotsTma slots of 16-byte rows (eight groups = four units, by TMA) or
-  // one slot per ring slot of 4-byte rows (the unit's two groups, by cp.async)
+  off += slots * rec_bytes(MT);
+  // scale / zero staging, [slot][mat][scale|zero][64 rows][row bytes]: either
+  // (sub-pipeline, quad slot) slots of 16-byte rows (eight groups = four units,
+  // by TMA) or one slot per ring slot of 4-byte rows (the unit's two groups)
   off = round_up(off, 128);
   L.sz = off;
-  off += NW * kSzSlotBytes;
-  L.red = off;  // [pair][mat][group][token][64 rows] fp32 shares of the current row block
-  off += kPairs * NW * 2 * MT * kRows * 4;
+  off += NW * sz_region_bytes(NW);
+  L.red = off;  // [pair][mat][token][64 rows] fp32 shares of the current row block
+  off += kPairs * NW * MT * kRows * 4;
   L.flag = off;  // "this CTA finishes the row block" broadcast
   off += 16;
-  L.bars = round_up(off, 8);  // full[stages], empty[stages]
-  off = L.bars + 2 * stages_of(NW) * 8;
+  L.bars = round_up(off, 8);  // full[slots], empty[slots]
+  off = L.bars + 2 * slots * 8;
   L.total = off + 1024;  // slack for aligning the base to 1024 B
   return L;
 }
@@ -243,38 +247,45 @@ __global__ void __maxnreg__(160)
   constexpr int MTp = mtp_of(MT);
   constexpr Layout L = make_layout<MT, NW>();
   constexpr uint32_t kRec = rec_bytes(MT);
+  constexpr int R = ring_of(NW);
+  constexpr int kSlots = kPairs * R;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* sm = smem_raw + (base - raw);  // generic pointer to the aligned base
 
-  const int cta = blockIdx.x;
-  const long long u0 = unit_begin(cta, p.U, p.P);
-  const long long u1 = unit_begin(cta + 1, p.U, p.P);
-  const int nu = (int)(u1 - u0);
-
-  const uint32_t full_bar = base + L.bars;
-  constexpr int kStages = stages_of(NW);
-  const uint32_t empty_bar = full_bar + kStages * 8;
-
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // this warp's sub-pipeline and its range of units (p.P ranges in all; a
+  // sub-pipeline of the last CTA may have none)
+  const int pair = warp < kConsumerWarps ? (warp >> 1) : (warp - kConsumerWarps);
+  const int vc = blockIdx.x * kPairs + pair;
+  const long long u0 = vc < p.P ? unit_begin(vc, p.U, p.P) : 0;
+  const long long u1 = vc < p.P ? unit_begin(vc + 1, p.U, p.P) : 0;
+  const int nu = (int)(u1 - u0);
+  const int rb0 = (int)(u0 / p.TS), st0 = (int)(u0 - (long long)rb0 * p.TS);
+
+  const uint32_t full_bar = base + L.bars;
+  const uint32_t empty_bar = full_bar + kSlots * 8;
 
   if (threadIdx.x == 0) {
 #pragma unroll
-    for (int s = 0; s < kStages; ++s) {
-      // the loader's expect_tx, plus 32 cp.async arrivals when scales / zeros use cp.async
+    for (int s = 0; s < kSlots; ++s) {
+      // the producer's expect_tx, plus 32 cp.async arrivals when scales / zeros use cp.async
       mbar_init(full_bar + 8 * s, p.sz_tma ? 1 : 1 + 32);
-      mbar_init(empty_bar + 8 * s, 2);  // the two warps of the unit's pair
+      mbar_init(empty_bar + 8 * s, 2);  // the sub-pipeline's two consumer warps
     }
     fence_barrier_init();
     griddep_launch_dependents();
   }
   __syncthreads();
 
+  // Quads: unit i of a range opens a quad when it is the range's first or
+  // st % 4 == 0 (a row block's first unit has st == 0).
   bool ok = true;
-  if (warp == kLoaderWarp) {
-    // -------------------------------------------------------------- loader
+  if (warp >= kConsumerWarps) {
+    // ---------------------------------------------------------- producer
+    const int pp = pair;
     if (lane == 0) {
       prefetch_tensormap(&tmap0);
       if (NW == 2) prefetch_tensormap(&tmap1);
@@ -289,18 +300,20 @@ __global__ void __maxnreg__(160)
     }
     const uint64_t pol = l2_policy_evict_first();
     const uint64_t pol_sz = l2_policy_evict_normal();
-    // Unit (slot, rb, st): its weight boxes and, when it opens a scale/zero
-    // quad (sz_slot >= 0), the quad's scale and zero boxes, all on the slot's
-    // full barrier.  The activation record is added after griddep_wait.
-    auto issue_unit = [&](int slot, int rb, int st, int sz_slot) {
+    // Weight boxes (and, when the unit opens a quad, the quad's scale / zero
+    // boxes) of local unit j, on its slot's full barrier; the activation
+    // record is added separately.
+    auto issue_unit = [&](int j, int rb, int st, bool opens_quad, int qs) {
+      const int slot = pp * R + j % R;
       const uint32_t fb = full_bar + 8 * slot;
-      mbar_arrive_expect_tx(fb, NW * kRows * 128 + kRec + (sz_slot >= 0 ? NW * 2 * kRows * 16 : 0));
+      const bool szq = p.sz_tma && opens_quad;
+      mbar_arrive_expect_tx(fb, NW * kRows * 128 + kRec + (szq ? NW * 2 * kRows * 16 : 0));
       tma_load_2d(base + L.w + (slot * NW + 0) * kRows * 128, &tmap0, st * kWordsPerStage, rb * kRows, fb, pol);
       if (NW == 2)
         tma_load_2d(base + L.w + (slot * NW + 1) * kRows * 128, &tmap1, st * kWordsPerStage, rb * kRows, fb,
                     pol);
-      if (sz_slot >= 0) {
-        const uint32_t d = base + L.sz + sz_slot * NW * (2 * kRows * 16);
+      if (szq) {
+        const uint32_t d = base + L.sz + (pp * kSzQuadSlots + qs) * NW * (2 * kRows * 16);
         const int gx = kSzQuadGroups * (st >> 2), gy = rb * kRows;
         tma_load_2d(d, &tms0, gx, gy, fb, pol_sz);
         tma_load_2d(d + kRows * 16, &tmz0, gx, gy, fb, pol_sz);
@@ -310,21 +323,14 @@ __global__ void __maxnreg__(160)
         }
       }
     };
-    // A unit opens a quad when it is the CTA's first or starts a group of four
-    // stages (quads never straddle row blocks: TS % 4 == 0 in this mode).
-    int sz_next = 0;  // next quad slot
-    auto quad_slot = [&](int i, int st) -> int {
-      if (!p.sz_tma || (i != 0 && (st & 3) != 0)) return -1;
-      const int q = sz_next;
-      sz_next = (sz_next + 1 == kSzSlotsTma) ? 0 : sz_next + 1;
-      return q;
-    };
-    // weights (and quads) of the first ring-full of units do not depend on the previous kernel
+    // pass 1, before the previous kernel has finished: the first ring-full of
+    // this sub-pipeline's weight (and quad) boxes
     {
-      int rb = (int)(u0 / p.TS), st = (int)(u0 - (long long)rb * p.TS);
-      for (int i = 0; i < min(nu, kStages); ++i) {
-        const int q = quad_slot(i, st);
-        if (lane == 0) issue_unit(i, rb, st, q);
+      int rb = rb0, st = st0, qs = kSzQuadSlots - 1;
+      for (int j = 0; j < nu && j < R; ++j) {
+        const bool oq = (j == 0) || ((st & 3) == 0);
+        if (oq) qs = (qs + 1 == kSzQuadSlots) ? 0 : qs + 1;
+        if (lane == 0) issue_unit(j, rb, st, oq, qs);
         if (++st == p.TS) {
           st = 0;
           ++rb;
@@ -333,41 +339,43 @@ __global__ void __maxnreg__(160)
     }
     griddep_wait();  // the activation records come from the x_prepare kernel
     fence_proxy_async_global();
-    int slot = 0;
-    uint32_t phase = 0;  // phase of the empty barrier awaited on this lap of the ring
-    int rb = (int)(u0 / p.TS), st = (int)(u0 - (long long)rb * p.TS);  // stepped per unit
-    for (int i = 0; i < nu; ++i) {
-      const uint32_t fb = full_bar + 8 * slot;
-      if (i >= kStages) {
-        if (!mbar_wait_bounded(empty_bar + 8 * slot, phase)) {
-          ok = false;
-          break;
-        }
-        const int q = quad_slot(i, st);
-        if (lane == 0) issue_unit(slot, rb, st, q);
-      }
-      if (lane == 0) bulk_load(base + L.x + slot * kRec, p.rec + (size_t)st * kRec, kRec, fb);
-      if (!p.sz_tma) {
-        // scale / zero pairs (groups 2st, 2st+1) of the 64 rows: 4 bytes each
-        const int row0 = rb * kRows;
+    // pass 2: records (and cp.async scales / zeros) for every unit, refilling
+    // slots as the consumers free them
+    {
+      int rb = rb0, st = st0, qs = kSzQuadSlots - 1;
+      for (int j = 0; j < nu; ++j) {
+        const bool oq = (j == 0) || ((st & 3) == 0);
+        {
+          if (oq) qs = (qs + 1 == kSzQuadSlots) ? 0 : qs + 1;
+          const int slot = pp * R + j % R;
+          const uint32_t fb = full_bar + 8 * slot;
+          if (j >= R) {
+            if (!mbar_wait_bounded(empty_bar + 8 * slot, ((j / R) - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) issue_unit(j, rb, st, oq, qs);
+          }
+          if (lane == 0) bulk_load(base + L.x + slot * kRec, p.rec + (size_t)st * kRec, kRec, fb);
+          if (!p.sz_tma) {
+            // scale / zero pairs (groups 2st, 2st+1) of the 64 rows: 4 bytes each
+            const int row0 = rb * kRows;
 #pragma unroll
-        for (int j = lane; j < NW * 2 * kRows; j += 32) {
-          const int mat = j / (2 * kRows);
-          const int arr = (j / kRows) & 1;
-          const int r = j % kRows;
-          const __half* src = mat == 0 ? (arr ? p.zeros0 : p.scales0) : (arr ? p.zeros1 : p.scales1);
-          src += (size_t)(row0 + r) * p.G + 2 * st;
-          cp_async_4(base + L.sz + (((slot * NW + mat) * 2 + arr) * kRows + r) * 4, src);
+            for (int e = lane; e < NW * 2 * kRows; e += 32) {
+              const int mat = e / (2 * kRows);
+              const int arr = (e / kRows) & 1;
+              const int r = e % kRows;
+              const __half* src = mat == 0 ? (arr ? p.zeros0 : p.scales0) : (arr ? p.zeros1 : p.scales1);
+              src += (size_t)(row0 + r) * p.G + 2 * st;
+              cp_async_4(base + L.sz + (((slot * NW + mat) * 2 + arr) * kRows + r) * 4, src);
+            }
+            cp_async_arrive_noinc(fb);
+          }
         }
-        cp_async_arrive_noinc(fb);
-      }
-      if (++slot == kStages) {
-        slot = 0;
-        if (i >= kStages) phase ^= 1u;  // laps after the first wait on alternating phases
-      }
-      if (++st == p.TS) {
-        st = 0;
-        ++rb;
+        if (++st == p.TS) {
+          st = 0;
+          ++rb;
+        }
       }
     }
     cp_async_wait<0>();  // no copy may land after this CTA exits
@@ -376,8 +384,8 @@ __global__ void __maxnreg__(160)
     griddep_wait();  // the row-block counters are cleared by x_prepare
     const int tid = threadIdx.x;  // 0 .. kConsumerThreads-1
     const int g = lane >> 2, t = lane & 3;
-    const int pair = warp >> 1;  // takes the units i of this CTA with i % kPairs == pair
-    const int G = warp & 1;      // which quantisation group of those units this warp takes
+    const int G = warp & 1;  // which quantisation group of its units this warp takes
+    const int ptid = tid & 63;  // thread index within the pair
     // Lane (g, t) covers rows pg + 8h, h = 0..7 (tile h/2, MMA row g or g+8): the
     // permutation keeps the swizzled reads conflict-free, and because every such
     // row is pg mod 8 the 128-byte swizzle maps chunk 4G+t to one column for all.
@@ -391,12 +399,11 @@ __global__ void __maxnreg__(160)
 #pragma unroll
     for (int qq = 0; qq < 4; ++qq) x_off[qq] = L.x + frag_offset(MT, G, gc, t, qq);
     const uint32_t xs_off = L.x + rec_frag_bytes(MT) + (G * MTp + tok2) * 4;
-    // scale/zero staging: 16-byte rows (quad of four units) or 4-byte rows (one unit)
+    // scale/zero staging: 16-byte rows (quad slots) or 4-byte rows (ring slots)
     const uint32_t rs = p.sz_tma ? 16u : 4u;
     const uint32_t sz_mat = 2 * kRows * rs;  // bytes per (slot, mat)
     const uint32_t sz_lane = L.sz + pg * rs;
     const int half_shift = 16 * G;  // this group's fp16 within a scale/zero pair
-    int sz_slot = -1;
     float acc[NW][kRowTiles][4];
 #pragma unroll
     for (int mat = 0; mat < NW; ++mat)
@@ -405,22 +412,16 @@ __global__ void __maxnreg__(160)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[mat][tl][j] = 0.f;
 
-    int slot = 0;
-    uint32_t phase = 0;
-    const int rb0 = (int)(u0 / p.TS);
-    int rb = rb0, st = (int)(u0 - (long long)rb0 * p.TS);  // stepped per unit
-    for (int i = 0; i < nu; ++i) {
-      // the scale/zero slot of unit i (same sequence as the loader's)
-      if (!p.sz_tma) {
-        sz_slot = slot;
-      } else if (i == 0 || (st & 3) == 0) {
-        sz_slot = (sz_slot + 1 == kSzSlotsTma) ? 0 : sz_slot + 1;
-      }
-      if ((i & (kPairs - 1)) == pair) {
+    int rb = rb0, st = st0, qs = kSzQuadSlots - 1;
+    for (int j = 0; j < nu; ++j) {
+      const bool oq = (j == 0) || ((st & 3) == 0);
+      {
+        if (oq) qs = (qs + 1 == kSzQuadSlots) ? 0 : qs + 1;
+        const int slot = pair * R + j % R;
         // After a wait gives up, later waits are skipped (the result is garbage
         // and the status word is set) but every warp still takes the same path
         // through the row-block barriers below, so none of them can hang.
-        if (ok && !mbar_wait_bounded(full_bar + 8 * slot, phase)) ok = false;
+        if (ok && !mbar_wait_bounded(full_bar + 8 * slot, (j / R) & 1)) ok = false;
         const uint32_t xso = slot * kRec;                // this slot's activation record
         const uint32_t wso = slot * (NW * kRows * 128);  // this slot's weight boxes
         // B fragments: token g, K values 128G + 32t + 8qq + {j, j+4}
@@ -436,6 +437,7 @@ __global__ void __maxnreg__(160)
         }
         // group sums of x for tokens 2t and 2t+1
         const float2 xs = ld_smem<float2>(sm, xs_off + xso);
+        const uint32_t sz_slot = p.sz_tma ? (uint32_t)(pair * kSzQuadSlots + qs) : (uint32_t)slot;
         const uint32_t sz_col = p.sz_tma ? (uint32_t)(st & 3) * 4u : 0u;
 #pragma unroll
         for (int mat = 0; mat < NW; ++mat) {
@@ -459,7 +461,7 @@ __global__ void __maxnreg__(160)
 #pragma unroll
           for (int tl = 0; tl < kRowTiles; ++tl)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) d[tl][j] = 0.f;
+            for (int e = 0; e < 4; ++e) d[tl][e] = 0.f;
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq) {
 #pragma unroll
@@ -489,72 +491,68 @@ __global__ void __maxnreg__(160)
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar + 8 * slot);
       }
-      if (++slot == kStages) {
-        slot = 0;
-        phase ^= 1u;
-      }
 
       // ------------------------------------------- end of a row-block run
-      const bool run_ends = (i + 1 == nu) || (st + 1 == p.TS);
+      const bool run_ends = (j + 1 == nu) || (st + 1 == p.TS);
       if (run_ends) {
-        // every warp's share: red[pair][mat][G][token][row]
+        const int bar = 2 + pair;  // the pair's named barrier (64 threads)
+        float* red = reinterpret_cast<float*>(sm + L.red) + pair * NW * MT * kRows;  // [mat][token][row]
+        // the pair's share: group 0 stores, group 1 adds (a fixed order)
 #pragma unroll
-        for (int mat = 0; mat < NW; ++mat) {
+        for (int gg = 0; gg < 2; ++gg) {
+          if (G == gg) {
 #pragma unroll
-          for (int tl = 0; tl < kRowTiles; ++tl) {
+            for (int mat = 0; mat < NW; ++mat) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int tok = 2 * t + (j & 1);
-              const int row = 16 * tl + pg + ((j < 2) ? 0 : 8);
-              if (tok < MT)
-                *reinterpret_cast<float*>(sm + L.red + ((((pair * NW + mat) * 2 + G) * MT + tok) * kRows + row) * 4) =
-                    acc[mat][tl][j];
-              acc[mat][tl][j] = 0.f;
+              for (int tl = 0; tl < kRowTiles; ++tl) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int tok = 2 * t + (e & 1);
+                  const int row = 16 * tl + pg + ((e < 2) ? 0 : 8);
+                  float* dst = red + (mat * MT + tok) * kRows + row;
+                  if (tok < MT) *dst = (gg == 0 ? 0.f : *dst) + acc[mat][tl][e];
+                  acc[mat][tl][e] = 0.f;
+                }
+              }
             }
           }
+          named_barrier(bar, 64);
         }
-        named_barrier(1, kConsumerThreads);
         const long long rb_lo = (long long)rb * p.TS, rb_hi = rb_lo + p.TS;
         const int nout = p.M * kRows;
-        // the eight shares of an output, added in a fixed order
-        auto reduced = [&](int mat, int tok, int row) {
-          float v = 0.f;
-#pragma unroll
-          for (int q = 0; q < kPairs * 2; ++q)
-            v += ld_smem<float>(sm, L.red + ((((q >> 1) * NW + mat) * 2 + (q & 1)) * MT + tok) * kRows * 4 + row * 4);
-          return v;
-        };
         if (u0 <= rb_lo && u1 >= rb_hi) {
-          // the whole row block was ours
-          for (int o = tid; o < nout; o += kConsumerThreads) {
+          // the whole row block was this range's
+          for (int o = ptid; o < nout; o += 64) {
             const int tok = o / kRows, row = o - tok * kRows;
             float v[NW];
 #pragma unroll
-            for (int mat = 0; mat < NW; ++mat) v[mat] = reduced(mat, tok, row);
+            for (int mat = 0; mat < NW; ++mat) v[mat] = red[(mat * MT + tok) * kRows + row];
             store_out<EPI, NW>(p.y, (size_t)tok * p.N + (size_t)rb * kRows + row, v);
           }
         } else {
-          // publish this CTA's partial; the last of the row block's CTAs finishes it
-          float* mine = p.partials + (2LL * cta + (rb == rb0 ? 0 : 1)) * slot_floats(MT, NW);
-          for (int o = tid; o < nout; o += kConsumerThreads) {
+          // publish this range's partial; the last of the row block's ranges finishes it
+          float* mine = p.partials + (2LL * vc + (rb == rb0 ? 0 : 1)) * slot_floats(MT, NW);
+          for (int o = ptid; o < nout; o += 64) {
             const int tok = o / kRows, row = o - tok * kRows;
 #pragma unroll
-            for (int mat = 0; mat < NW; ++mat) mine[(mat * MT + tok) * kRows + row] = reduced(mat, tok, row);
+            for (int mat = 0; mat < NW; ++mat)
+              mine[(mat * MT + tok) * kRows + row] = red[(mat * MT + tok) * kRows + row];
           }
           __threadfence();
-          named_barrier(1, kConsumerThreads);
+          named_barrier(bar, 64);
           const int c_first = unit_owner(rb_lo, p.U, p.P), c_last = unit_owner(rb_hi - 1, p.U, p.P);
-          if (tid == 0) {
+          int* flag = reinterpret_cast<int*>(sm + L.flag) + pair;
+          if (ptid == 0) {
             const unsigned int prev = atomicAdd(p.counters + rb, 1u);
-            *reinterpret_cast<int*>(sm + L.flag) = (prev == (unsigned int)(c_last - c_first));
+            *flag = (prev == (unsigned int)(c_last - c_first));
           }
-          named_barrier(1, kConsumerThreads);
-          if (ld_smem<int>(sm, L.flag)) {
+          named_barrier(bar, 64);
+          if (*flag) {
             __threadfence();
-            // Partial slots: a CTA after c_first began inside this row block (slot
-            // 2c); c_first used slot 2c + 1 unless it began exactly at rb_lo.
+            // Partial slots: a range after c_first began inside this row block
+            // (slot 2c); c_first used slot 2c + 1 unless it began exactly at rb_lo.
             const long long first_slot = 2LL * c_first + (unit_begin(c_first, p.U, p.P) == rb_lo ? 0 : 1);
-            for (int o = tid; o < nout; o += kConsumerThreads) {
+            for (int o = ptid; o < nout; o += 64) {
               const int tok = o / kRows, row = o - tok * kRows;
               float v[NW];
 #pragma unroll
@@ -563,25 +561,25 @@ __global__ void __maxnreg__(160)
               for (int cb = c_first; cb <= c_last; cb += kSumBatch) {
                 float part[kSumBatch][NW];
 #pragma unroll
-                for (int j = 0; j < kSumBatch; ++j) {
-                  const int c = cb + j;
+                for (int e = 0; e < kSumBatch; ++e) {
+                  const int c = cb + e;
                   const long long ps = c == c_first ? first_slot : 2LL * (c <= c_last ? c : cb);
                   const float* src = p.partials + ps * slot_floats(MT, NW);
 #pragma unroll
                   for (int mat = 0; mat < NW; ++mat)
-                    part[j][mat] = c <= c_last ? __ldcg(src + (mat * MT + tok) * kRows + row) : 0.f;
+                    part[e][mat] = c <= c_last ? __ldcg(src + (mat * MT + tok) * kRows + row) : 0.f;
                 }
 #pragma unroll
-                for (int j = 0; j < kSumBatch; ++j)
+                for (int e = 0; e < kSumBatch; ++e)
 #pragma unroll
-                  for (int mat = 0; mat < NW; ++mat) v[mat] += part[j][mat];
+                  for (int mat = 0; mat < NW; ++mat) v[mat] += part[e][mat];
               }
               store_out<EPI, NW>(p.y, (size_t)tok * p.N + (size_t)rb * kRows + row, v);
             }
-            if (tid == 0) p.counters[rb] = 0u;
+            if (ptid == 0) p.counters[rb] = 0u;
           }
         }
-        named_barrier(1, kConsumerThreads);  // red is rewritten by the next run
+        named_barrier(bar, 64);  // red and the flag are rewritten by the next run
       }
       if (++st == p.TS) {
         st = 0;
@@ -720,15 +718,15 @@ int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
   if (rc) return rc;
   static const int min_units = [] {
     const char* e = getenv("FOCAL_W4A16_MIN_UNITS");  // tuning override
-    return e && atoi(e) > 0 ? atoi(e) : kMinUnitsPerCta;
+    return e && atoi(e) > 0 ? atoi(e) : kMinUnitsPerRange;
   }();
-  static const int waves = [] {
-    const char* e = getenv("FOCAL_W4A16_WAVES");  // tuning override: CTAs per resident slot
-    return e && atoi(e) > 0 ? std::min(atoi(e), kMaxCtasPerSm) : 1;
-  }();
-  p.P = (int)std::min<long long>((p.U + min_units - 1) / min_units,
-                                 (long long)std::min(occ * waves, kMaxCtasPerSm) * dev.sm_count);
+  // p.P unit ranges, kPairs per CTA, all CTAs resident at once; every range
+  // gets at least one unit (p.P <= U) so each row block's owners all report.
+  (void)occ;  // the carve-up and register cap leave room for one CTA per SM
+  static_assert(kPairs <= kMaxCtasPerSm, "workspace bound assumes at most kMaxCtasPerSm ranges per SM");
+  p.P = (int)std::min<long long>((p.U + min_units - 1) / min_units, (long long)kPairs * dev.sm_count);
   p.P = std::max(p.P, 1);
+  const int grid = (p.P + kPairs - 1) / kPairs;
   const WsLayout W = ws_layout(MT, NW, p.TS, p.RB, p.P);
   if (ws_bytes < W.total)
     return set_error(FOCAL_ERR_WORKSPACE, "workspace too small: need %zu bytes, got %zu", W.total, ws_bytes);
@@ -738,7 +736,7 @@ int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
   rc = launch_prepare<MT>(x, workspace + W.rec, p.counters, p.M, p.K, p.RB, stream);
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.P, 1, 1);
+  cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = stream;
