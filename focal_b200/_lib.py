@@ -30,6 +30,7 @@ SIGNATURES = {
     "focal_w4a16_check_shape": (_I, [_I, _I, _I]),
     "focal_w4a16_workspace_size": (_S, [_I, _I, _I]),
     "focal_w4a16_gemv": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
+    "focal_w4a16_gemv_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "focal_w4a16_gemv_f32": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
     "focal_w4a16_gate_up_silu": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
     "focal_w4a16_dequant": (_I, [_P, _P, _P, _P, _I, _I, _P]),

@@ -824,6 +824,13 @@ int run(int epi, const void* x, const int32_t* wq0, const void* s0, const void* 
   return dispatch_mt<2, kEpiSiluMul>(MT, maps, p, xb, ws, ws_bytes, dev, stream);
 }
 
+// Fixed device scratch for callers that cannot allocate a workspace: one
+// 8 MiB array per device, its address resolved once per device.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[64] = {};
+
 }  // namespace gemv
 }  // namespace focal
 
@@ -865,6 +872,35 @@ int focal_w4a16_gate_up_silu(const void* x, const int32_t* wq_gate, const void* 
                              size_t ws_bytes, cudaStream_t stream) {
   return gemv::run(gemv::kEpiSiluMul, x, wq_gate, scales_gate, zeros_gate, wq_up, scales_up,
                    zeros_up, h, M, K, N, workspace, ws_bytes, stream);
+}
+
+int focal_w4a16_gemv_noalloc(const void* x, const int32_t* wq, const void* scales, const void* zeros,
+                             void* y, int M, int K, int N, cudaStream_t stream) {
+  clear_error();
+  int rc = gemv::check_shape(M, K, N);
+  if (rc) return rc;
+  const size_t need = focal_w4a16_workspace_size(M, K, N);
+  if (need > gemv::kNoAllocScratchBytes)
+    return set_error(FOCAL_ERR_UNSUPPORTED,
+                     "focal_w4a16_gemv_noalloc: M=%d K=%d N=%d needs %zu bytes of scratch, more than its "
+                     "fixed %zu; call focal_w4a16_gemv with a workspace instead",
+                     M, K, N, need, gemv::kNoAllocScratchBytes);
+  int dev = 0;
+  rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return set_error(FOCAL_ERR_INVALID_VALUE, "device %d out of range", dev);
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(gemv::g_noalloc_mutex);
+    if (!gemv::g_noalloc_ptr[dev]) {
+      rc = check_cuda(cudaGetSymbolAddress(&gemv::g_noalloc_ptr[dev], gemv::g_noalloc_scratch),
+                      "cudaGetSymbolAddress");
+      if (rc) return rc;
+    }
+    scratch = gemv::g_noalloc_ptr[dev];
+  }
+  return gemv::run(gemv::kEpiBf16, x, wq, scales, zeros, nullptr, nullptr, nullptr, y, M, K, N, scratch,
+                   gemv::kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"

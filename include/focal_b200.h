@@ -72,6 +72,22 @@ int focal_w4a16_gemv(const void* x, const int32_t* wq, const void* scales, const
                      void* y, int M, int K, int N, void* workspace, size_t ws_bytes,
                      cudaStream_t stream);
 
+/* The linear layer without a caller workspace.  No reference counterpart: for
+ * callers that cannot allocate device memory where they call it (a host
+ * callback, or a runtime whose device memory is planned up front), it uses a
+ * fixed 8 MiB scratch array per device instead.
+ *  - Shapes whose focal_w4a16_workspace_size() exceeds 8 MiB are rejected with
+ *    FOCAL_ERR_UNSUPPORTED (with M = 8 that admits K up to 217600, with M = 1
+ *    up to about 3.7 million, on a 148-SM device).
+ *  - The first call on a device resolves the scratch's address
+ *    (cudaGetSymbolAddress); make it before any stream capture.
+ *  - Nothing in the scratch has to start at zero: each call clears what it uses.
+ *  - All calls on one device share the scratch, so calls that may overlap
+ *    (different streams, or host threads without ordering) race; order them on
+ *    one stream. */
+int focal_w4a16_gemv_noalloc(const void* x, const int32_t* wq, const void* scales, const void* zeros,
+                             void* y, int M, int K, int N, cudaStream_t stream);
+
 /* Same product with an fp32 output (no bf16 rounding): the partial sum of a
  * K-sharded (row-parallel) projection before its all-reduce.  New entry point;
  * the reference has no multi-GPU path. */

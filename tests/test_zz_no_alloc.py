@@ -1,0 +1,57 @@
+"""focal_w4a16_gemv_noalloc: the linear layer with its fixed per-device scratch
+instead of a caller workspace, called through the C ABI.
+
+Collected last (file name) and independent of what ran before: the scratch
+needs no initial state.  Each case makes two calls in a row on different inputs
+and compares each with focal_w4a16_gemv (caller workspace) and the oracle.
+"""
+import numpy as np
+import pytest
+import torch
+
+from focal_b200 import _lib
+from oracle import w4a16 as ow
+from tests import _capi as C
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def noalloc(x, wq, scales, zeros):
+    M, K = x.shape
+    N = wq.shape[0]
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    _lib.call("focal_w4a16_gemv_noalloc", C.ptr(x), C.ptr(wq), C.ptr(scales), C.ptr(zeros), C.ptr(y),
+              M, K, N, C.stream_ptr())
+    return y
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 4096), (8, 8192, 11008), (4, 11008, 4096), (2, 8192, 8192)])
+def test_noalloc_matches_workspace_entry_point(cuda, M, K, N):
+    outs = []
+    for call in range(2):
+        x, wq, s, z = ow.baseline_case(M, K, N, seed=4000 + 10 * M + call)
+        dx, dwq, ds, dz = C.to_dev_bf16(x, cuda), C.to_dev(wq, cuda), C.to_dev(s, cuda), C.to_dev(z, cuda)
+        y_na = noalloc(dx, dwq, ds, dz)
+        y_ws = C.gemv(dx, dwq, ds, dz)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(y_na.float(), y_ws.float(), atol=ATOL, rtol=RTOL)
+        ref = ow.bf16_to_f32(ow.linear(x, wq, s, z))
+        np.testing.assert_allclose(y_na.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
+        outs.append(y_na)
+    # the second call did not disturb the first call's result
+    assert not torch.equal(outs[0], outs[1])
+
+
+def test_noalloc_rejects_shapes_beyond_its_scratch(cuda):
+    M, K, N = 8, 1 << 20, 64  # needs more than the 8 MiB scratch
+    x = torch.zeros((M, K), dtype=torch.bfloat16, device=cuda)
+    wq = torch.zeros((N, K // 8), dtype=torch.int32, device=cuda)
+    s = torch.zeros((N, K // 128), dtype=torch.float16, device=cuda)
+    z = torch.zeros_like(s)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
+    rc = _lib.lib().focal_w4a16_gemv_noalloc(C.ptr(x), C.ptr(wq), C.ptr(s), C.ptr(z), C.ptr(y), M, K, N,
+                                             C.stream_ptr())
+    assert rc == _lib.FOCAL_ERR_UNSUPPORTED
+    assert "scratch" in _lib.last_error()
