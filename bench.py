@@ -295,7 +295,7 @@ def e2e_sweep(cases, steps, device):
     dy = [torch.empty((M, N), dtype=torch.bfloat16, device=device) for (M, K, N) in SWEEP]
     hy = [torch.empty((M, N), dtype=torch.bfloat16).pin_memory() for (M, K, N) in SWEEP]
     ws_n = max(int(L.focal_w4a16_workspace_size(M, K, N)) for (M, K, N) in SWEEP)
-    ws = torch.empty(ws_n, dtype=torch.uint8, device=device)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device=device)  # zeroed once, as the C ABI requires
 
     def step():
         for i, (M, K, N) in enumerate(SWEEP):

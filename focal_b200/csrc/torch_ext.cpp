@@ -15,7 +15,9 @@
 #include <cmath>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
+#include <vector>
 
 #include "focal_b200.h"
 
@@ -35,11 +37,31 @@ cudaStream_t current_stream() {
   return reinterpret_cast<cudaStream_t>(at::cuda::getCurrentCUDAStream().stream());
 }
 
-// Per-call W4A16 workspace from PyTorch's caching allocator (stream-ordered,
-// so a block freed after this call is only reused by later work on the stream).
+// Device workspaces, one per (kind, device, stream), zeroed when allocated.
+// Their counters start at zero and every successful call leaves them at zero,
+// and calls on one stream are ordered, so reuse is safe.  A workspace that is
+// outgrown stays allocated (a CUDA graph captured earlier may still use it).
+enum WsKind { kWsLinear = 0, kWsAttention = 1 };
+std::mutex g_ws_mutex;
+std::map<std::tuple<int, int, cudaStream_t>, torch::Tensor> g_ws;
+std::vector<torch::Tensor> g_ws_retired;
+
+torch::Tensor workspace_for(WsKind kind, const torch::Device& dev, cudaStream_t stream, size_t bytes) {
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  auto key = std::make_tuple((int)kind, (int)dev.index(), stream);
+  auto it = g_ws.find(key);
+  if (it == g_ws.end() || (size_t)it->second.numel() < bytes) {
+    if (it != g_ws.end()) g_ws_retired.push_back(it->second);
+    auto t = torch::zeros({(int64_t)bytes}, torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+    g_ws[key] = t;
+    return t;
+  }
+  return it->second;
+}
+
 torch::Tensor w4a16_workspace(const torch::Tensor& x, int64_t N) {
   const size_t n = focal_w4a16_workspace_size((int)x.size(0), (int)x.size(1), (int)N);
-  return torch::empty({(int64_t)std::max<size_t>(n, 16)}, x.options().dtype(torch::kUInt8));
+  return workspace_for(kWsLinear, x.device(), current_stream(), std::max<size_t>(n, 256));
 }
 
 // Validation in the reference's order and wording (csrc/w4a16_gemv.cu:157-177).
@@ -141,24 +163,6 @@ torch::Tensor pack_int4(torch::Tensor q) {
   return wq;
 }
 
-// Split-KV workspace, one per (device, stream): its counters start at zero
-// (torch::zeros) and every successful call leaves them at zero, and calls on
-// one stream are ordered, so reuse is safe.
-std::mutex g_ws_mutex;
-std::map<std::pair<int, cudaStream_t>, torch::Tensor> g_ws;
-
-torch::Tensor workspace_for(const torch::Device& dev, cudaStream_t stream, size_t bytes) {
-  std::lock_guard<std::mutex> lock(g_ws_mutex);
-  auto key = std::make_pair((int)dev.index(), stream);
-  auto it = g_ws.find(key);
-  if (it == g_ws.end() || (size_t)it->second.numel() < bytes) {
-    auto t = torch::zeros({(int64_t)bytes}, torch::TensorOptions().dtype(torch::kUInt8).device(dev));
-    g_ws[key] = t;
-    return t;
-  }
-  return it->second;
-}
-
 torch::Tensor gqa_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                    c10::optional<double> scale) {
   check_tensor(q, "q", at::kBFloat16);
@@ -181,7 +185,7 @@ torch::Tensor gqa_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch
   void* ws = nullptr;
   torch::Tensor ws_t;
   if (ws_bytes > 0) {
-    ws_t = workspace_for(q.device(), stream, ws_bytes);
+    ws_t = workspace_for(kWsAttention, q.device(), stream, ws_bytes);
     ws = ws_t.data_ptr();
   }
   raise_on(focal_gqa_decode_attn(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(),

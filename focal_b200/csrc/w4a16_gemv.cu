@@ -5,30 +5,28 @@
 // Replaces the reference's SIMT kernel and launcher (csrc/w4a16_gemv.cu:33-116,
 // :152-223) behind the same packing and dequant semantics (README.md:66-73).
 //
-// Two kernels per call, chained with programmatic dependent launch:
+// One kernel per call, launched with programmatic dependent launch so that its
+// CTAs start streaming weights while the previous kernel finishes.
 //
-// 1. x_prepare (O(M*K) work, once per call): the activations in the order of
-//    the tensor core's B fragments plus their fp32 sums per 128-wide group,
-//    one 16-byte-aligned record per 256 K values, into the caller's
-//    workspace; it also clears the row-block arrival counters.
-//
-// 2. w4a16_gemv, stream-K over units of (64 weight rows x 256 K values), one
-//    resident CTA per SM made of four independent sub-pipelines.  The units
-//    are cut into P contiguous ranges (four per CTA), so every range streams
-//    the same number of bytes in a single wave.  Sub-pipeline p of a CTA owns
-//    one range, a ring of 3 slots (gate/up: 2), producer warp 8 + p and
-//    consumer warps 2p, 2p + 1; separate rings keep one slow box from
-//    stalling the other loads in flight, as a single in-order ring would.
+// w4a16_gemv, stream-K over units of (64 weight rows x 256 K values), one
+// resident CTA per SM made of four independent sub-pipelines.  The units are
+// cut into P contiguous ranges (four per CTA), so every range streams the same
+// number of bytes in a single wave.  Sub-pipeline p of a CTA owns one range, a
+// ring of 3 slots (gate/up: 2), producer warp 8 + p and consumer warps 2p,
+// 2p + 1; separate rings keep one slow box from stalling the other loads in
+// flight, as a single in-order ring would.
 //    * the producer fills its ring.  Per unit: the packed weights as one 2-D
-//      TMA box of 64 rows x 128 bytes (128-byte swizzle), the unit's
-//      activation record as one bulk copy, and the fp16 scales and zeros:
+//      TMA box of 64 rows x 128 bytes (128-byte swizzle), the fp16 scales and
+//      zeros (below), and the unit's activation record, which the warp builds
+//      itself from x (the tensor core's B fragments for the unit's 256 K
+//      values plus fp32 sums per 128-wide group).  Scales and zeros:
 //      when K % 1024 == 0, one 2-D TMA box each of 64 rows x 8 groups per
 //      four units (a "quad", two quad slots per sub-pipeline), otherwise the
 //      unit's two groups per row with 4-byte cp.async.  All complete on the
 //      slot's mbarrier.  The first ring-full of weight and scale/zero boxes
 //      is issued before the previous kernel has finished (weights, scales and
 //      zeros must not be written by a kernel that triggers programmatic
-//      launch early); only the activation copies wait for it.
+//      launch early); only the activation records wait for it.
 //    * the two consumer warps take one quantisation group each of every
 //      unit, over all 64 rows (four 16-row MMA tiles sharing one load of the
 //      group's activation fragments).  A packed word becomes bf16 (128 + q)
@@ -63,7 +61,6 @@ constexpr int kRows = 16 * kRowTiles;   // weight rows per unit
 // consumer warps 2p, 2p + 1 (one per quantisation group of a unit).
 constexpr int kPairs = 4;
 constexpr int kConsumerWarps = 2 * kPairs;
-constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kThreads = 32 * (kConsumerWarps + kPairs);
 // One resident CTA per SM (12 warps at up to 160 registers): 12 x 8 KB (gate/up:
 // 8 x 16 KB) of weights in flight.
@@ -107,67 +104,30 @@ __host__ __device__ constexpr uint32_t frag_offset(int MT, int G, int g, int t, 
 }
 
 // ------------------------------------------------- workspace layout
-// [records: TS x rec_bytes][counters: RB x 4, padded to 256][partials: 2P slots]
+// [row-block arrival counters: kMaxRowBlocks x 4 B][partials: 2P slots].  The
+// counters sit at the same place for every shape, start at zero and are left
+// at zero by every call (the range that finishes a row block clears its
+// counter), so one workspace serves calls of any shape in turn.
+constexpr int kMaxRowBlocks = 4096;  // N <= 262144
+constexpr size_t kCounterBytes = (size_t)kMaxRowBlocks * 4;
 struct WsLayout {
-  size_t rec, counters, partials, total;
+  size_t counters, partials, total;
 };
 
 __host__ __device__ inline size_t slot_floats(int MT, int NW) { return (size_t)NW * MT * kRows; }
 
-inline WsLayout ws_layout(int MT, int NW, int TS, int RB, int P) {
+inline WsLayout ws_layout(int MT, int NW, int P) {
   WsLayout w;
-  w.rec = 0;
-  w.counters = (size_t)TS * rec_bytes(MT);
-  w.partials = w.counters + ((size_t)RB * 4 + 255) / 256 * 256;
+  w.counters = 0;
+  w.partials = kCounterBytes;
   w.total = w.partials + 2 * (size_t)P * slot_floats(MT, NW) * 4;
   return w;
 }
 
-struct PrepParams {
-  const __nv_bfloat16* x;
-  uint8_t* rec;
-  unsigned int* counters;
-  int M, K, stages, RB;
-};
-
-// One warp per (unit column, token): lane l takes K values 8l..8l+7.
-template <int MT>
-__global__ void __launch_bounds__(128) x_prepare_kernel(const PrepParams p) {
-  griddep_launch_dependents();
-  griddep_wait();  // x may be the previous kernel's output; the workspace may still be read by it
-  constexpr int MTp = mtp_of(MT);
-  if (blockIdx.x == 0)
-    for (int r = threadIdx.x; r < p.RB; r += blockDim.x) p.counters[r] = 0u;
-  const int lane = threadIdx.x & 31;
-  const int item = blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (item >= p.stages * MTp) return;
-  const int st = item / MTp, m = item - st * MTp;
-  uint8_t* rec = p.rec + (size_t)st * rec_bytes(MT);
-  uint4 v = make_uint4(0u, 0u, 0u, 0u);
-  if (m < p.M)
-    v = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)m * p.K + (size_t)st * kStageK) + lane);
-  float sum = bf16_lo(v.x) + bf16_hi(v.x) + bf16_lo(v.y) + bf16_hi(v.y) + bf16_lo(v.z) + bf16_hi(v.z) +
-              bf16_lo(v.w) + bf16_hi(v.w);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-  const int G = lane >> 4, c = lane & 15;
-  if (c == 0) reinterpret_cast<float*>(rec + rec_frag_bytes(MT))[G * MTp + m] = sum;
-  if (m < MT) {
-    uint4 pv;
-    pv.x = prmt(v.x, v.z, 0x5410);
-    pv.y = prmt(v.x, v.z, 0x7632);
-    pv.z = prmt(v.y, v.w, 0x5410);
-    pv.w = prmt(v.y, v.w, 0x7632);
-    *reinterpret_cast<uint4*>(rec + frag_offset(MT, G, m, c >> 2, c & 3)) = pv;
-  }
-}
-
 // ------------------------------------------------------------------ GEMV
 struct Params {
-  const uint8_t* rec;      // activation records (x_prepare output)
-  unsigned int* counters;  // per row block arrivals (cleared by x_prepare)
+  const __nv_bfloat16* x;  // activations [M, K]
+  unsigned int* counters;  // per row block arrivals (zero between calls)
   float* partials;         // [2P][NW][MT][64] split row-block partial sums
   const __half* scales0;
   const __half* zeros0;
@@ -271,8 +231,9 @@ __global__ void __maxnreg__(160)
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int s = 0; s < kSlots; ++s) {
-      // the producer's expect_tx, plus 32 cp.async arrivals when scales / zeros use cp.async
-      mbar_init(full_bar + 8 * s, p.sz_tma ? 1 : 1 + 32);
+      // the producer's expect_tx and its activation-record arrival, plus 32
+      // cp.async arrivals when scales / zeros use cp.async
+      mbar_init(full_bar + 8 * s, p.sz_tma ? 2 : 2 + 32);
       mbar_init(empty_bar + 8 * s, 2);  // the sub-pipeline's two consumer warps
     }
     fence_barrier_init();
@@ -302,12 +263,12 @@ __global__ void __maxnreg__(160)
     const uint64_t pol_sz = l2_policy_evict_normal();
     // Weight boxes (and, when the unit opens a quad, the quad's scale / zero
     // boxes) of local unit j, on its slot's full barrier; the activation
-    // record is added separately.
+    // record is written separately.
     auto issue_unit = [&](int j, int rb, int st, bool opens_quad, int qs) {
       const int slot = pp * R + j % R;
       const uint32_t fb = full_bar + 8 * slot;
       const bool szq = p.sz_tma && opens_quad;
-      mbar_arrive_expect_tx(fb, NW * kRows * 128 + kRec + (szq ? NW * 2 * kRows * 16 : 0));
+      mbar_arrive_expect_tx(fb, NW * kRows * 128 + (szq ? NW * 2 * kRows * 16 : 0));
       tma_load_2d(base + L.w + (slot * NW + 0) * kRows * 128, &tmap0, st * kWordsPerStage, rb * kRows, fb, pol);
       if (NW == 2)
         tma_load_2d(base + L.w + (slot * NW + 1) * kRows * 128, &tmap1, st * kWordsPerStage, rb * kRows, fb,
@@ -337,12 +298,47 @@ __global__ void __maxnreg__(160)
         }
       }
     }
-    griddep_wait();  // the activation records come from the x_prepare kernel
-    fence_proxy_async_global();
+    griddep_wait();  // x may be the previous kernel's output
+    // Activation record of stage st, written by the warp into the slot: for
+    // each token m the B fragments of K values 256st + 8l .. 8l + 7 (lane l),
+    // then the fp32 sums of the two 128-wide groups.  x is a few KB to a few
+    // hundred KB and shared by every CTA, so these loads hit L2; each unit's
+    // slice is loaded one unit ahead so their latency stays off the ring.
+    auto load_x = [&](uint4 (&v)[MTp], int st) {
+#pragma unroll
+      for (int m = 0; m < MTp; ++m) {
+        v[m] = make_uint4(0u, 0u, 0u, 0u);
+        if (m < p.M)
+          v[m] = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)m * p.K + (size_t)st * kStageK) + lane);
+      }
+    };
+    auto write_record = [&](uint8_t* rec, const uint4 (&v)[MTp]) {
+      const int Gq = lane >> 4, c = lane & 15;
+#pragma unroll
+      for (int m = 0; m < MTp; ++m) {
+        float sum = bf16_lo(v[m].x) + bf16_hi(v[m].x) + bf16_lo(v[m].y) + bf16_hi(v[m].y) + bf16_lo(v[m].z) +
+                    bf16_hi(v[m].z) + bf16_lo(v[m].w) + bf16_hi(v[m].w);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        if (c == 0) reinterpret_cast<float*>(rec + rec_frag_bytes(MT))[Gq * MTp + m] = sum;
+        if (m < MT) {
+          uint4 pv;
+          pv.x = prmt(v[m].x, v[m].z, 0x5410);
+          pv.y = prmt(v[m].x, v[m].z, 0x7632);
+          pv.z = prmt(v[m].y, v[m].w, 0x5410);
+          pv.w = prmt(v[m].y, v[m].w, 0x7632);
+          *reinterpret_cast<uint4*>(rec + frag_offset(MT, Gq, m, c >> 2, c & 3)) = pv;
+        }
+      }
+    };
     // pass 2: records (and cp.async scales / zeros) for every unit, refilling
     // slots as the consumers free them
     {
       int rb = rb0, st = st0, qs = kSzQuadSlots - 1;
+      uint4 xcur[MTp], xnext[MTp];
+      if (nu > 0) load_x(xcur, st0);
       for (int j = 0; j < nu; ++j) {
         const bool oq = (j == 0) || ((st & 3) == 0);
         {
@@ -356,7 +352,12 @@ __global__ void __maxnreg__(160)
             }
             if (lane == 0) issue_unit(j, rb, st, oq, qs);
           }
-          if (lane == 0) bulk_load(base + L.x + slot * kRec, p.rec + (size_t)st * kRec, kRec, fb);
+          if (j + 1 < nu) load_x(xnext, st + 1 == p.TS ? 0 : st + 1);
+          write_record(sm + L.x + slot * kRec, xcur);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(fb);  // the record's arrival (release: orders the writes above)
+#pragma unroll
+          for (int m = 0; m < MTp; ++m) xcur[m] = xnext[m];
           if (!p.sz_tma) {
             // scale / zero pairs (groups 2st, 2st+1) of the 64 rows: 4 bytes each
             const int row0 = rb * kRows;
@@ -381,7 +382,7 @@ __global__ void __maxnreg__(160)
     cp_async_wait<0>();  // no copy may land after this CTA exits
   } else {
     // ------------------------------------------------------------ consumers
-    griddep_wait();  // the row-block counters are cleared by x_prepare
+    griddep_wait();  // the previous call on this workspace has finished with its counters
     const int tid = threadIdx.x;  // 0 .. kConsumerThreads-1
     const int g = lane >> 2, t = lane & 3;
     const int G = warp & 1;  // which quantisation group of its units this warp takes
@@ -646,7 +647,7 @@ int mt_for(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
 int check_shape(int M, int K, int N) {
   if (M < 1 || M > 8) return set_error(FOCAL_ERR_UNSUPPORTED, "unsupported M");
-  if (N <= 0 || N % 64 != 0) return set_error(FOCAL_ERR_UNSUPPORTED, "unsupported N");
+  if (N <= 0 || N % 64 != 0 || N > kRows * kMaxRowBlocks) return set_error(FOCAL_ERR_UNSUPPORTED, "unsupported N");
   // The reference accepts only a whitelist (csrc/w4a16_gemv.cu:135-143); this
   // contract is rule-based but keeps its deliberate K = N = 11008 rejection.
   if (K <= 0 || K % kStageK != 0 || K > (1 << 24) || (K == 11008 && N == 11008))
@@ -661,7 +662,7 @@ size_t workspace_bound(int M, int K, int N, int sm_count) {
   const int TS = K / kStageK, RB = N / kRows;
   const long long U = (long long)TS * RB;
   const int P = (int)std::min<long long>(U, (long long)kMaxCtasPerSm * sm_count);
-  return ws_layout(mt_for(M), 2, TS, RB, P).total;
+  return ws_layout(mt_for(M), 2, P).total;
 }
 
 cudaLaunchAttribute pdl_attribute() {
@@ -689,21 +690,6 @@ int ctas_per_sm(const void* kern, int slot, int smem, int dev, int* out) {
   return FOCAL_OK;
 }
 
-template <int MT>
-int launch_prepare(const __nv_bfloat16* x, uint8_t* rec, unsigned int* counters, int M, int K, int RB,
-                   cudaStream_t stream) {
-  PrepParams pp{x, rec, counters, M, K, K / kStageK, RB};
-  const int items = pp.stages * mtp_of(MT);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((items + 3) / 4, 1, 1);
-  cfg.blockDim = dim3(128, 1, 1);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1] = {pdl_attribute()};
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, x_prepare_kernel<MT>, pp), "x_prepare_kernel launch");
-}
-
 template <int MT, int NW, int EPI>
 int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
              uint8_t* workspace, size_t ws_bytes, const DeviceInfo& dev, cudaStream_t stream) {
@@ -727,14 +713,12 @@ int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
   p.P = (int)std::min<long long>((p.U + min_units - 1) / min_units, (long long)kPairs * dev.sm_count);
   p.P = std::max(p.P, 1);
   const int grid = (p.P + kPairs - 1) / kPairs;
-  const WsLayout W = ws_layout(MT, NW, p.TS, p.RB, p.P);
+  const WsLayout W = ws_layout(MT, NW, p.P);
   if (ws_bytes < W.total)
     return set_error(FOCAL_ERR_WORKSPACE, "workspace too small: need %zu bytes, got %zu", W.total, ws_bytes);
-  p.rec = workspace + W.rec;
   p.counters = reinterpret_cast<unsigned int*>(workspace + W.counters);
   p.partials = reinterpret_cast<float*>(workspace + W.partials);
-  rc = launch_prepare<MT>(x, workspace + W.rec, p.counters, p.M, p.K, p.RB, stream);
-  if (rc) return rc;
+  p.x = x;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);

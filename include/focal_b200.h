@@ -48,7 +48,7 @@ int focal_abi_version(void);
  *   scales fp16  [N, K/128]  4-byte aligned
  *   zeros  fp16  [N, K/128]  4-byte aligned
  *   dequant: w[n,k] = (float(q) - float(zeros[n,k/128])) * float(scales[n,k/128])
- * Contract: 1 <= M <= 8; N % 64 == 0; 0 < K <= 2^24 with K % 256 == 0;
+ * Contract: 1 <= M <= 8; N % 64 == 0, N <= 262144; 0 < K <= 2^24 with K % 256 == 0;
  * K = N = 11008 is rejected ("unsupported K/N") as the reference does.
  */
 
@@ -56,13 +56,14 @@ int focal_abi_version(void);
  * reference's message.  Replaces check_shape, csrc/w4a16_gemv.cu:129-149. */
 int focal_w4a16_check_shape(int M, int K, int N);
 
-/* Bytes of device workspace the three linear entry points below need for
- * (M, K, N) on the current device: the activations rearranged once per call
- * into the tensor cores' fragment order with their per-group sums (about
- * 2*M*K bytes), one arrival counter per 64 output rows, and the partial sums
- * of row blocks that several CTAs share.  0 if the shape is outside the
- * contract.  The workspace needs 256-byte alignment and no initialisation
- * (each call clears what it uses); calls that share one must be ordered on a
+/* Bytes of device workspace the linear entry points below need for (M, K, N)
+ * on the current device: 16 KB of arrival counters (one per 64 output rows,
+ * N <= 262144) followed by the fp32 partial sums of row blocks that several
+ * CTAs share.  0 if the shape is outside the contract.  The workspace needs
+ * 256-byte alignment and must be zeroed once before its first call; every
+ * call that returns FOCAL_OK leaves the counters at zero again, so one
+ * workspace can serve calls of any shape (zero it again after a call that
+ * failed on the device).  Calls that share a workspace must be ordered on one
  * stream. */
 size_t focal_w4a16_workspace_size(int M, int K, int N);
 
@@ -77,11 +78,14 @@ int focal_w4a16_gemv(const void* x, const int32_t* wq, const void* scales, const
  * callback, or a runtime whose device memory is planned up front), it uses a
  * fixed 8 MiB scratch array per device instead.
  *  - Shapes whose focal_w4a16_workspace_size() exceeds 8 MiB are rejected with
- *    FOCAL_ERR_UNSUPPORTED (with M = 8 that admits K up to 217600, with M = 1
- *    up to about 3.7 million, on a 148-SM device).
+ *    FOCAL_ERR_UNSUPPORTED (on a 148-SM B200 every shape of the contract fits;
+ *    the check guards devices with many more SMs).
  *  - The first call on a device resolves the scratch's address
  *    (cudaGetSymbolAddress); make it before any stream capture.
- *  - Nothing in the scratch has to start at zero: each call clears what it uses.
+ *  - The scratch's arrival counters start at zero when the library loads and
+ *    every successful call leaves them at zero; after a call that failed on the
+ *    device (focal_device_status nonzero) the results of later calls are not
+ *    defined until the process restarts.
  *  - All calls on one device share the scratch, so calls that may overlap
  *    (different streams, or host threads without ordering) race; order them on
  *    one stream. */

@@ -29,8 +29,9 @@ def to_dev(a: np.ndarray, device) -> torch.Tensor:
 
 
 def w4a16_workspace(M, K, N, device):
+    """A fresh workspace: zeroed, as the C ABI requires before its first use."""
     n = int(_lib.lib().focal_w4a16_workspace_size(M, K, N))
-    return torch.empty(max(n, 256), dtype=torch.uint8, device=device), n
+    return torch.zeros(max(n, 256), dtype=torch.uint8, device=device), n
 
 
 def gemv(x, wq, scales, zeros, out_dtype=torch.bfloat16, ws=None):

@@ -1,9 +1,11 @@
 """focal_w4a16_gemv_noalloc: the linear layer with its fixed per-device scratch
 instead of a caller workspace, called through the C ABI.
 
-Collected last (file name) and independent of what ran before: the scratch
-needs no initial state.  Each case makes two calls in a row on different inputs
-and compares each with focal_w4a16_gemv (caller workspace) and the oracle.
+For callers that cannot allocate device memory where they call the layer.
+Collected last (file name) and independent of what ran before: the scratch's
+counters start at zero when the library loads and every call leaves them at
+zero.  Each case makes two calls in a row on different inputs and compares each
+with focal_w4a16_gemv (caller workspace) and the oracle.
 """
 import numpy as np
 import pytest
@@ -42,16 +44,3 @@ def test_noalloc_matches_workspace_entry_point(cuda, M, K, N):
         outs.append(y_na)
     # the second call did not disturb the first call's result
     assert not torch.equal(outs[0], outs[1])
-
-
-def test_noalloc_rejects_shapes_beyond_its_scratch(cuda):
-    M, K, N = 8, 1 << 20, 64  # needs more than the 8 MiB scratch
-    x = torch.zeros((M, K), dtype=torch.bfloat16, device=cuda)
-    wq = torch.zeros((N, K // 8), dtype=torch.int32, device=cuda)
-    s = torch.zeros((N, K // 128), dtype=torch.float16, device=cuda)
-    z = torch.zeros_like(s)
-    y = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
-    rc = _lib.lib().focal_w4a16_gemv_noalloc(C.ptr(x), C.ptr(wq), C.ptr(s), C.ptr(z), C.ptr(y), M, K, N,
-                                             C.stream_ptr())
-    assert rc == _lib.FOCAL_ERR_UNSUPPORTED
-    assert "scratch" in _lib.last_error()
