@@ -144,6 +144,13 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// Atomic add with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* addr, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
 // ------------------------------------------------------------ cp.async (LDGSTS)
 // 16-byte copy global -> shared, bypassing L1 (.cg).
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {

@@ -539,17 +539,19 @@ __global__ void __maxnreg__(160)
             for (int mat = 0; mat < NW; ++mat)
               mine[(mat * MT + tok) * kRows + row] = red[(mat * MT + tok) * kRows + row];
           }
-          __threadfence();
+          // The barrier orders the pair's partial stores before thread 0's
+          // acquire-release increment, which publishes them at GPU scope; in
+          // the range that finishes the row block the same increment (acquire)
+          // and the barrier after it order the loads of every partial.
           named_barrier(bar, 64);
           const int c_first = unit_owner(rb_lo, p.U, p.P), c_last = unit_owner(rb_hi - 1, p.U, p.P);
           int* flag = reinterpret_cast<int*>(sm + L.flag) + pair;
           if (ptid == 0) {
-            const unsigned int prev = atomicAdd(p.counters + rb, 1u);
+            const unsigned int prev = atom_add_acq_rel_gpu(p.counters + rb, 1u);
             *flag = (prev == (unsigned int)(c_last - c_first));
           }
           named_barrier(bar, 64);
           if (*flag) {
-            __threadfence();
             // Partial slots: a range after c_first began inside this row block
             // (slot 2c); c_first used slot 2c + 1 unless it began exactly at rb_lo.
             const long long first_slot = 2LL * c_first + (unit_begin(c_first, p.U, p.P) == rb_lo ? 0 : 1);
