@@ -151,6 +151,13 @@ __device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* addr,
   return old;
 }
 
+// Atomic add on a shared-memory word with acquire-release semantics at CTA scope.
+__device__ __forceinline__ unsigned int atom_add_acq_rel_cta_shared(uint32_t addr, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(addr), "r"(v) : "memory");
+  return old;
+}
+
 // ------------------------------------------------------------ cp.async (LDGSTS)
 // 16-byte copy global -> shared, bypassing L1 (.cg).
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {

@@ -37,9 +37,11 @@
 //      so the tensor core only sees exact small integers and x.
 //    * at the end of each row block's run in a range the two warps' shares
 //      are added (group 0 then group 1) and the sub-pipeline either writes y
-//      (its range held the whole row block) or stores its fp32 partial; the
-//      last range to arrive on the row block's counter adds all partials in
-//      range order (deterministic, no waiting) and writes y.
+//      (its range held the whole row block), or, when the CTA's four ranges
+//      are exactly the row block, leaves its share in shared memory for the
+//      last of the four to add, or stores its fp32 partial in the workspace;
+//      the last range to arrive on the row block's counter adds all partials
+//      in range order (deterministic, no waiting) and writes y.
 //    No TMA multicast is used.
 #include <algorithm>
 #include <cmath>
@@ -165,8 +167,8 @@ __host__ __device__ constexpr Layout make_layout() {
   off += NW * sz_region_bytes(NW);
   L.red = off;  // [pair][mat][token][64 rows] fp32 shares of the current row block
   off += kPairs * NW * MT * kRows * 4;
-  L.flag = off;  // "this CTA finishes the row block" broadcast
-  off += 16;
+  L.flag = off;  // per pair "finish the row block" broadcast, then the CTA's arrival counter
+  off += 32;
   L.bars = round_up(off, 8);  // full[slots], empty[slots]
   off = L.bars + 2 * slots * 8;
   L.total = off + 1024;  // slack for aligning the base to 1024 B
@@ -236,6 +238,7 @@ __global__ void __maxnreg__(160)
       mbar_init(full_bar + 8 * s, p.sz_tma ? 2 : 2 + 32);
       mbar_init(empty_bar + 8 * s, 2);  // the sub-pipeline's two consumer warps
     }
+    *reinterpret_cast<unsigned int*>(sm + L.flag + 16) = 0u;  // in-CTA row-block arrivals
     fence_barrier_init();
     griddep_launch_dependents();
   }
@@ -529,6 +532,30 @@ __global__ void __maxnreg__(160)
 #pragma unroll
             for (int mat = 0; mat < NW; ++mat) v[mat] = red[(mat * MT + tok) * kRows + row];
             store_out<EPI, NW>(p.y, (size_t)tok * p.N + (size_t)rb * kRows + row, v);
+          }
+        } else if (4 * (int)blockIdx.x + 3 < p.P && rb_lo == unit_begin(4 * blockIdx.x, p.U, p.P) &&
+                   rb_hi == unit_begin(4 * blockIdx.x + 4, p.U, p.P)) {
+          // This CTA's four ranges are exactly this row block (so each pair has
+          // this one run): the last pair to arrive adds the four shares from
+          // shared memory in pair order.  The pair barrier orders its share
+          // before thread 0's acquire-release increment; the last pair's
+          // increment and barrier order its reads after all four.
+          int* flag = reinterpret_cast<int*>(sm + L.flag) + pair;
+          if (ptid == 0) *flag = (atom_add_acq_rel_cta_shared(base + L.flag + 16, 1u) == kPairs - 1);
+          named_barrier(bar, 64);
+          if (*flag) {
+            for (int o = ptid; o < nout; o += 64) {
+              const int tok = o / kRows, row = o - tok * kRows;
+              float v[NW];
+#pragma unroll
+              for (int mat = 0; mat < NW; ++mat) {
+                v[mat] = 0.f;
+#pragma unroll
+                for (int q = 0; q < kPairs; ++q)
+                  v[mat] += reinterpret_cast<const float*>(sm + L.red)[((q * NW + mat) * MT + tok) * kRows + row];
+              }
+              store_out<EPI, NW>(p.y, (size_t)tok * p.N + (size_t)rb * kRows + row, v);
+            }
           }
         } else {
           // publish this range's partial; the last of the row block's ranges finishes it

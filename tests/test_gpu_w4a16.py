@@ -97,8 +97,9 @@ def test_gemv_contract_shapes(cuda, K, N):
         assert_parity(y, ref[:M], f"M={M} K={K} N={N}")
 
 
-def test_gemv_f32_output_matches_exact_sum(cuda):
-    x, wq, s, z = ow.baseline_case(8, 4096, 4096, seed=5)
+@pytest.mark.parametrize("K,N", [(4096, 4096), (8192, 4096)])
+def test_gemv_f32_output_matches_exact_sum(cuda, K, N):
+    x, wq, s, z = ow.baseline_case(8, K, N, seed=5)
     y = C.gemv(*dev_case(x, wq, s, z, cuda), out_dtype=torch.float32).cpu().numpy().astype(np.float64)
     exact = ow.linear_f64(x, wq, s, z)
     err = np.abs(y - exact).max(axis=1) / np.linalg.norm(exact, axis=1)
@@ -151,9 +152,12 @@ def silu_mul_oracle(g_bits, u_bits):
     return ow.f32_to_bf16(sg * u)
 
 
-@pytest.mark.parametrize("M", [1, 4, 8])
-def test_gate_up_silu_fused(cuda, M):
-    K, N = 4096, 11008
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 11008), (4, 4096, 11008), (8, 4096, 11008),
+                                   (2, 4096, 4096), (8, 4096, 8192)])
+def test_gate_up_silu_fused(cuda, M, K, N):
+    """K=4096 with N <= 8192 puts every 64-row block in one CTA (reduced in
+    shared memory); N=11008 splits row blocks across CTAs (reduced in global
+    memory)."""
     x, wg, sg, zg = ow.baseline_case(M, K, N, seed=900 + M)
     _, wu, su, zu = ow.baseline_case(1, K, N, seed=950 + M)
     ref = silu_mul_oracle(ow.linear(x, wg, sg, zg), ow.linear(x, wu, su, zu))
