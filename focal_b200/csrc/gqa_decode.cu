@@ -96,15 +96,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(empty_bar + 8 * s, kConsumerWarps);
     }
     fence_barrier_init();
+    griddep_launch_dependents();
   }
   __syncthreads();
+  // Launched with programmatic dependent launch: the set-up above overlaps the
+  // previous kernel; q, the caches and the workspace are touched only after it.
+  if (warp == kConsumerWarps && lane == 0) {
+    prefetch_tensormap(&tmap_k);
+    prefetch_tensormap(&tmap_v);
+  }
+  griddep_wait();
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
     bool ok = true;
     if (lane == 0) {
-      prefetch_tensormap(&tmap_k);
-      prefetch_tensormap(&tmap_v);
       const uint64_t pol = l2_policy_evict_first();
       for (int i = 0; i < nt; ++i) {
         const int slot = i % kStages;
@@ -294,14 +300,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   // ---- split combine by the last CTA of this (b, kv head)
   named_barrier(1, kConsumerWarps * 32);
+  // The barrier orders this CTA's partial stores before thread 0's
+  // acquire-release increment, which publishes them at GPU scope; in the last
+  // CTA the same increment and the barrier after it order its loads.
   if (ctid == 0) {
-    __threadfence();
-    const unsigned int prev = atomicAdd(p.counters + bh, 1u);
+    const unsigned int prev = atom_add_acq_rel_gpu(p.counters + bh, 1u);
     *last_flag = (prev == (unsigned int)(p.splits - 1));
   }
   named_barrier(1, kConsumerWarps * 32);
   if (!*last_flag) return;
-  __threadfence();
   for (int e = ctid; e < nvals; e += kConsumerWarps * 32) {
     const int row = e / (kD / 4);
     const int d = (e - row * (kD / 4)) * 4;
@@ -440,9 +447,17 @@ int focal_gqa_decode_attn(const void* q, const void* k, const void* v, void* o, 
 
   rc = ensure_dynamic_smem(reinterpret_cast<const void*>(attn::gqa_decode_kernel), 40, attn::kSmemBytes);
   if (rc) return rc;
-  dim3 grid(pl.splits, bhn, 1);
-  attn::gqa_decode_kernel<<<grid, attn::kThreads, attn::kSmemBytes, stream>>>(mk, mv, p);
-  return check_cuda(cudaGetLastError(), "gqa_decode_kernel launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.splits, bhn, 1);
+  cfg.blockDim = dim3(attn::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = attn::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, attn::gqa_decode_kernel, mk, mv, p), "gqa_decode_kernel launch");
 }
 
 }  // extern "C"
