@@ -29,6 +29,7 @@ With --gpus N under torchrun each rank runs its own sweep replica (weak scaling)
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import re
@@ -493,15 +494,22 @@ def run_tp70b(args, rank, world, local):
     row = [F.baseline_case(1, k2, N2, seed=20_000 + 100 * rank + c, device=device)[1:] for c in range(copies)]
     x = F.baseline_case(M, K1, 64, seed=5, device=device)[0]
 
-    def layer(c, collectives=True):
+    group = tp.TpGroup(max_m=M, max_n=max(n1, N2), device=device)
+
+    def layer(c, mode):
+        if mode == "fused":  # one kernel per projection, the collective inside it
+            y = group.allgather_linear(x, *col[c])
+            return group.allreduce_linear(y[:, rank * k2:(rank + 1) * k2].contiguous(), *row[c])
+        collectives = mode == "nccl"
         y_local = F.w4a16_linear(x, *col[c])
         y = tp.gather_columns(y_local) if collectives else y_local
         x2 = y[:, rank * k2:(rank + 1) * k2].contiguous() if collectives else y_local
         part = F.w4a16_linear_f32(x2, *row[c])
         return tp.reduce_partials(part) if collectives else part
 
+    modes = ("fused", "nccl", "local")
     graphs = {}
-    for mode in (True, False):
+    for mode in modes:
         for c in range(copies):
             layer(c, mode)
         torch.cuda.synchronize()
@@ -517,7 +525,7 @@ def run_tp70b(args, rank, world, local):
     reps = max(1, args.steps // copies)
     res = {}
     clk_summary = None
-    for mode in (True, False):
+    for mode in modes:
         for _ in range(max(3, args.warmup // copies + 1)):
             graphs[mode].replay()
         barrier(dist, device)
@@ -530,29 +538,42 @@ def run_tp70b(args, rank, world, local):
             e1.record()
             torch.cuda.synchronize(device)
         barrier(dist, device)
-        if mode:
+        if mode == "fused":
             clk_summary = clk.summary()
         res[mode] = max_over_ranks(e0.elapsed_time(e1) / (reps * copies), dist, device)
+    status = ctypes.c_int(-1)
+    from focal_b200 import _lib as flib
+
+    flib.lib().focal_device_status(status)
+    if status.value != 0:
+        raise RuntimeError(f"rank {rank}: device status {status.value} after the fused layers")
     if rank == 0:
-        ms, ms_k = res[True], res[False]
+        ms, ms_k, ms_n = res["fused"], res["local"], res["nccl"]
         line = {
             "metric": METRIC, "value": round(world * per_rank / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "n_gpus": world, "steps": reps * copies, "warmup": args.warmup, "ms_per_step": round(ms, 5),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int4xbf16->f32", "data": "synthetic",
             "config": {"workload": "tp70b_decode_layer", "M": M, "column": [K1, N1], "row": [K2, N2],
-                       "parallelism": f"tp{world}", "collectives": "bf16 all-gather + fp32 all-reduce (NCCL)",
+                       "parallelism": f"tp{world}",
+                       "collectives": "bf16 all-gather + fp32 all-reduce inside the two GEMV kernels "
+                                      "(peer-memory stores over NVLink, epoch flags)",
                        "l2": f"cold: {copies} rotating weight copies per rank"},
             "kernel_only": {"value": round(world * per_rank / (ms_k * 1e-3) / 1e9, 2), "unit": "GB/s",
                             "ms_per_step": round(ms_k, 5),
                             "frac_of_aggregate_peak": round(per_rank / (ms_k * 1e-3) / 1e9 / peak, 4),
                             "peak_per_gpu": peak, "peak_kind": peak_kind},
             "collective_ms": round(ms - ms_k, 5),
+            "nccl_collectives": {"value": round(world * per_rank / (ms_n * 1e-3) / 1e9, 2), "unit": "GB/s",
+                                 "ms_per_step": round(ms_n, 5),
+                                 "how": "the same GEMVs with torch.distributed all_gather_into_tensor / "
+                                        "all_reduce (NCCL) between them"},
             "gpu_launches": 2 * reps * copies,
             "clocks": clk_summary,
         }
         print(json.dumps(line), flush=True)
     del graphs
+    group.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -23,6 +23,16 @@ _I = ctypes.c_int
 _S = ctypes.c_size_t
 _F = ctypes.c_float
 
+
+class TpComm(ctypes.Structure):
+    """struct focal_tp_comm: every rank's buffer as mapped in this process."""
+
+    _fields_ = [("peer", ctypes.c_void_p * 8), ("bytes", ctypes.c_size_t),
+                ("world", ctypes.c_int), ("rank", ctypes.c_int)]
+
+
+_C = ctypes.POINTER(TpComm)
+
 # name -> (restype, argtypes); mirrors include/focal_b200.h
 SIGNATURES = {
     "focal_last_error": (ctypes.c_char_p, []),
@@ -33,6 +43,13 @@ SIGNATURES = {
     "focal_w4a16_gemv_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "focal_w4a16_gemv_f32": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
     "focal_w4a16_gate_up_silu": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
+    "focal_tp_buffer_size": (_S, [_I, _I, _I]),
+    "focal_tp_buffer_create": (_I, [_S, ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_uint8)]),
+    "focal_tp_buffer_open": (_I, [ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(_P)]),
+    "focal_tp_buffer_close": (_I, [_P]),
+    "focal_tp_buffer_destroy": (_I, [_P]),
+    "focal_w4a16_gemv_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _C, _P, _S, _P]),
+    "focal_w4a16_gemv_allreduce": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _C, _P, _S, _P]),
     "focal_w4a16_dequant": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "focal_pack_int4": (_I, [_P, _P, _I, _I, _P]),
     "focal_gqa_decode_workspace_size": (_S, [_I, _I, _I, _I, _I]),

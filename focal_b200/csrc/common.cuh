@@ -17,6 +17,7 @@ namespace focal {
 enum DeviceStatus : int {
   kDevOk = 0,
   kDevWaitTimeout = 1,  // a bounded mbarrier wait gave up
+  kDevPeerTimeout = 2,  // a tensor-parallel peer did not signal in time
 };
 
 // ~2^31 SM cycles (about one second at 1.9 GHz) before a wait gives up.
@@ -156,6 +157,18 @@ __device__ __forceinline__ unsigned int atom_add_acq_rel_cta_shared(uint32_t add
   unsigned int old;
   asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(addr), "r"(v) : "memory");
   return old;
+}
+
+// 64-bit relaxed accesses at system scope: single-copy atomic when 8-byte
+// aligned, so a word written by a peer GPU over NVLink is read whole or not
+// at all, and never served from a stale L1 line.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* addr, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* addr) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+  return v;
 }
 
 // ------------------------------------------------------------ cp.async (LDGSTS)

@@ -46,6 +46,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -85,7 +86,35 @@ __host__ __device__ constexpr uint32_t sz_region_bytes(int NW) {
                                                                        : kPairs * ring_of(NW) * 2 * kRows * 4;
 }
 
-enum Epi : int { kEpiBf16 = 0, kEpiF32 = 1, kEpiSiluMul = 2 };
+// Epilogues: bf16 y, fp32 y, silu(gate) * up, and the two tensor-parallel
+// ones, which finish each 64-row block through peer memory: all-gather (the
+// bf16 block is stored into every rank's full output) and all-reduce (the fp32
+// block is stored into every rank's receive buffer, then each rank adds the
+// ranks' blocks in rank order and writes bf16 y).
+enum Epi : int { kEpiBf16 = 0, kEpiF32 = 1, kEpiSiluMul = 2, kEpiAllGather = 3, kEpiAllReduce = 4 };
+constexpr int kMaxTp = 8;  // ranks in a tensor-parallel group
+
+__host__ __device__ constexpr bool is_tp(int epi) { return epi == kEpiAllGather || epi == kEpiAllReduce; }
+
+// Peer-memory view of a tensor-parallel group.  Every rank holds one buffer of
+// the same layout: [state: 256 B][receive halves: 2 x world x M x N words of
+// 8 bytes].  Call number e (counted from 1 on every rank) uses half e & 1:
+// rank r stores each element of a finished row block into slot r of that half
+// on every other rank as one 64-bit word {payload, e} (fp32 bits for
+// all-reduce, bf16 bits for all-gather), and the finisher of the same row
+// block on each rank polls the words it needs until their upper half reads e.
+// The data carries its own flag, so no fence or separate flag is needed.  A
+// half is rewritten only two calls later, after every rank has finished the
+// call in between, which every rank only does after it has read the older
+// call's words.  state = [calls completed on this rank, CTAs done with this
+// call].
+constexpr size_t kTpStateBytes = 256;
+constexpr size_t kTpRecvOffset = kTpStateBytes;
+struct TpParams {
+  unsigned long long* recv[kMaxTp];  // each rank's receive halves, as mapped here
+  unsigned int* state;
+  int world, rank;
+};
 
 // ---------------------------------------------------- activation records
 // One record per unit column: [group G][token m][t][4 x 16 B] B fragments, then
@@ -139,6 +168,7 @@ struct Params {
   int* status;
   int M, K, N, G, TS, RB, P;
   int sz_tma;   // scales / zeros by TMA quads (needs G % 8 == 0 and 16-byte aligned bases)
+  TpParams tp;  // tensor-parallel epilogues only
   long long U;  // units = RB * TS
 };
 
@@ -200,6 +230,106 @@ __device__ __forceinline__ void store_out(void* y, size_t yi, const float (&v)[N
   }
 }
 
+// Output of finished row block rb, written by the 64 threads of the pair that
+// finished it: thread ptid owns row ptid of the block for every token, and
+// value(tok, row, v) yields the block's fp32 sums.  The tensor-parallel
+// epilogues first send the thread's elements to every other rank as
+// {payload, epoch} words (64-bit relaxed stores at system scope, over NVLink
+// for peers), keeping its own in registers, then poll (bounded) the words the
+// other ranks sent for the same elements.  All-gather writes each rank's bf16
+// block into its columns of y [M, N * world]; all-reduce adds the ranks' fp32
+// values in rank order (the same order on every rank, so all ranks get the
+// same bits) and rounds once to bf16.
+template <int MT, int EPI, int NW, class ValueFn>
+__device__ __forceinline__ void finish_block(const Params& p, int rb, int ptid, unsigned int e, ValueFn&& value) {
+  const size_t col = (size_t)rb * kRows + ptid;
+  if constexpr (!is_tp(EPI)) {
+    for (int tok = 0; tok < p.M; ++tok) {
+      float v[NW];
+      value(tok, ptid, v);
+      store_out<EPI, NW>(p.y, (size_t)tok * p.N + col, v);
+    }
+  } else {
+    static_assert(NW == 1, "tensor-parallel epilogues take one weight matrix");
+    float mine[MT];
+    unsigned long long word[MT];
+#pragma unroll
+    for (int i = 0; i < MT; ++i) {
+      mine[i] = 0.f;
+      if (i < p.M) {
+        float v[1];
+        value(i, ptid, v);
+        mine[i] = EPI == kEpiAllGather ? __bfloat162float(__float2bfloat16_rn(v[0])) : v[0];
+      }
+      const unsigned int payload = EPI == kEpiAllGather
+                                       ? (unsigned int)__bfloat16_as_ushort(__float2bfloat16_rn(mine[i]))
+                                       : __float_as_uint(mine[i]);
+      word[i] = ((unsigned long long)e << 32) | payload;
+    }
+    const size_t slab = (size_t)p.M * p.N;  // words per (half, source rank)
+    const size_t half = (size_t)(e & 1u) * p.tp.world * slab;
+#pragma unroll
+    for (int q = 0; q < kMaxTp; ++q) {
+      if (q < p.tp.world && q != p.tp.rank) {
+        unsigned long long* dst = p.tp.recv[q] + half + (size_t)p.tp.rank * slab + col;
+#pragma unroll
+        for (int i = 0; i < MT; ++i)
+          if (i < p.M) st_relaxed_sys_u64(dst + (size_t)i * p.N, word[i]);
+      }
+    }
+    const unsigned long long* here = p.tp.recv[p.tp.rank] + half + col;
+    float acc[MT];
+    bool timed_out = false;
+    for (int src = 0; src < p.tp.world; ++src) {
+      float val[MT];
+      if (src == p.tp.rank) {
+#pragma unroll
+        for (int i = 0; i < MT; ++i) val[i] = mine[i];
+      } else {
+        const unsigned long long* r = here + (size_t)src * slab;
+        unsigned long long w[MT];
+#pragma unroll
+        for (int i = 0; i < MT; ++i) w[i] = i < p.M ? ld_relaxed_sys_u64(r + (size_t)i * p.N) : word[i];
+        const long long t0 = clock64();
+        while (!timed_out) {
+          bool ready = true;
+#pragma unroll
+          for (int i = 0; i < MT; ++i) ready = ready && (unsigned int)(w[i] >> 32) == e;
+          if (ready) break;
+          if (clock64() - t0 > kWaitLimitCycles) {
+            timed_out = true;  // the rest of this block is skipped: its output is garbage
+            atomicExch(p.status, kDevPeerTimeout);
+            break;
+          }
+#pragma unroll
+          for (int i = 0; i < MT; ++i)
+            if ((unsigned int)(w[i] >> 32) != e) w[i] = ld_relaxed_sys_u64(r + (size_t)i * p.N);
+        }
+#pragma unroll
+        for (int i = 0; i < MT; ++i)
+          val[i] = EPI == kEpiAllGather
+                       ? __bfloat162float(__ushort_as_bfloat16((unsigned short)(w[i] & 0xFFFFu)))
+                       : __uint_as_float((unsigned int)w[i]);
+      }
+      if (EPI == kEpiAllGather) {
+#pragma unroll
+        for (int i = 0; i < MT; ++i)
+          if (i < p.M)
+            static_cast<__nv_bfloat16*>(p.y)[((size_t)i * p.tp.world + src) * p.N + col] =
+                __float2bfloat16_rn(val[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < MT; ++i) acc[i] = src == 0 ? val[i] : acc[i] + val[i];
+      }
+    }
+    if (EPI == kEpiAllReduce) {
+#pragma unroll
+      for (int i = 0; i < MT; ++i)
+        if (i < p.M) static_cast<__nv_bfloat16*>(p.y)[(size_t)i * p.N + col] = __float2bfloat16_rn(acc[i]);
+    }
+  }
+}
+
 template <int MT, int NW, int EPI>
 __global__ void __maxnreg__(160)
     w4a16_gemv_kernel(const __grid_constant__ CUtensorMap tmap0, const __grid_constant__ CUtensorMap tmap1,
@@ -247,6 +377,7 @@ __global__ void __maxnreg__(160)
   // Quads: unit i of a range opens a quad when it is the range's first or
   // st % 4 == 0 (a row block's first unit has st == 0).
   bool ok = true;
+  unsigned int tp_e = 0;  // this call's tensor-parallel epoch (consumer threads)
   if (warp >= kConsumerWarps) {
     // ---------------------------------------------------------- producer
     const int pp = pair;
@@ -386,6 +517,7 @@ __global__ void __maxnreg__(160)
   } else {
     // ------------------------------------------------------------ consumers
     griddep_wait();  // the previous call on this workspace has finished with its counters
+    if constexpr (is_tp(EPI)) tp_e = __ldcg(p.tp.state) + 1u;  // written by the previous call's last CTA
     const int tid = threadIdx.x;  // 0 .. kConsumerThreads-1
     const int g = lane >> 2, t = lane & 3;
     const int G = warp & 1;  // which quantisation group of its units this warp takes
@@ -526,13 +658,10 @@ __global__ void __maxnreg__(160)
         const int nout = p.M * kRows;
         if (u0 <= rb_lo && u1 >= rb_hi) {
           // the whole row block was this range's
-          for (int o = ptid; o < nout; o += 64) {
-            const int tok = o / kRows, row = o - tok * kRows;
-            float v[NW];
+          finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](int tok, int row, float(&v)[NW]) {
 #pragma unroll
             for (int mat = 0; mat < NW; ++mat) v[mat] = red[(mat * MT + tok) * kRows + row];
-            store_out<EPI, NW>(p.y, (size_t)tok * p.N + (size_t)rb * kRows + row, v);
-          }
+          });
         } else if (4 * (int)blockIdx.x + 3 < p.P && rb_lo == unit_begin(4 * blockIdx.x, p.U, p.P) &&
                    rb_hi == unit_begin(4 * blockIdx.x + 4, p.U, p.P)) {
           // This CTA's four ranges are exactly this row block (so each pair has
@@ -544,9 +673,7 @@ __global__ void __maxnreg__(160)
           if (ptid == 0) *flag = (atom_add_acq_rel_cta_shared(base + L.flag + 16, 1u) == kPairs - 1);
           named_barrier(bar, 64);
           if (*flag) {
-            for (int o = ptid; o < nout; o += 64) {
-              const int tok = o / kRows, row = o - tok * kRows;
-              float v[NW];
+            finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](int tok, int row, float(&v)[NW]) {
 #pragma unroll
               for (int mat = 0; mat < NW; ++mat) {
                 v[mat] = 0.f;
@@ -554,8 +681,7 @@ __global__ void __maxnreg__(160)
                 for (int q = 0; q < kPairs; ++q)
                   v[mat] += reinterpret_cast<const float*>(sm + L.red)[((q * NW + mat) * MT + tok) * kRows + row];
               }
-              store_out<EPI, NW>(p.y, (size_t)tok * p.N + (size_t)rb * kRows + row, v);
-            }
+            });
           }
         } else {
           // publish this range's partial; the last of the row block's ranges finishes it
@@ -582,9 +708,7 @@ __global__ void __maxnreg__(160)
             // Partial slots: a range after c_first began inside this row block
             // (slot 2c); c_first used slot 2c + 1 unless it began exactly at rb_lo.
             const long long first_slot = 2LL * c_first + (unit_begin(c_first, p.U, p.P) == rb_lo ? 0 : 1);
-            for (int o = ptid; o < nout; o += 64) {
-              const int tok = o / kRows, row = o - tok * kRows;
-              float v[NW];
+            finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](int tok, int row, float(&v)[NW]) {
 #pragma unroll
               for (int mat = 0; mat < NW; ++mat) v[mat] = 0.f;
               // fixed order (deterministic sums); loads issued a batch at a time
@@ -604,8 +728,7 @@ __global__ void __maxnreg__(160)
 #pragma unroll
                   for (int mat = 0; mat < NW; ++mat) v[mat] += part[e][mat];
               }
-              store_out<EPI, NW>(p.y, (size_t)tok * p.N + (size_t)rb * kRows + row, v);
-            }
+            });
             if (ptid == 0) p.counters[rb] = 0u;
           }
         }
@@ -619,6 +742,14 @@ __global__ void __maxnreg__(160)
   }
 
   if (!ok && p.status) atomicExch(p.status, kDevWaitTimeout);
+  if constexpr (is_tp(EPI)) {
+    // the last CTA to finish advances this rank's epoch for the next call
+    __syncthreads();
+    if (threadIdx.x == 0 && atom_add_acq_rel_gpu(p.tp.state + 1, 1u) == gridDim.x - 1) {
+      p.tp.state[1] = 0u;
+      p.tp.state[0] = tp_e;
+    }
+  }
 }
 
 // ----------------------------------------------------------------- host side
@@ -703,11 +834,12 @@ cudaLaunchAttribute pdl_attribute() {
 
 // Resident CTAs per SM for one kernel instantiation (cached per device).
 std::mutex g_occ_mutex;
-int g_occ[64][12];
+constexpr int kOccSlots = 20;
+int g_occ[64][kOccSlots];
 
 int ctas_per_sm(const void* kern, int slot, int smem, int dev, int* out) {
   std::lock_guard<std::mutex> lock(g_occ_mutex);
-  if (dev < 0 || dev >= 64 || slot < 0 || slot >= 12) return set_error(FOCAL_ERR_INVALID_VALUE, "bad slot");
+  if (dev < 0 || dev >= 64 || slot < 0 || slot >= kOccSlots) return set_error(FOCAL_ERR_INVALID_VALUE, "bad slot");
   if (!g_occ[dev][slot]) {
     int n = 0;
     int rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem),
@@ -725,7 +857,7 @@ int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
   constexpr Layout L = make_layout<MT, NW>();
   static_assert(L.total <= 227 * 1024, "shared-memory carve-up exceeds the per-CTA limit");
   auto kern = w4a16_gemv_kernel<MT, NW, EPI>;
-  constexpr int slot = (MT == 1 ? 0 : MT == 2 ? 1 : MT == 4 ? 2 : 3) + 4 * EPI;
+  constexpr int slot = (MT == 1 ? 0 : MT == 2 ? 1 : MT == 4 ? 2 : 3) + 4 * EPI;  // < kOccSlots
   int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), slot, (int)L.total);
   if (rc) return rc;
   int occ = 0;
@@ -771,12 +903,97 @@ int dispatch_mt(int MT, const CUtensorMap* maps, const Params& p, const __nv_bfl
   }
 }
 
+// Bytes of one rank's tensor-parallel buffer for calls up to max_m x max_n.
+size_t tp_buffer_bytes(int world, int max_m, int max_n) {
+  return kTpRecvOffset + 2 * (size_t)world * max_m * max_n * 8;
+}
+
+// Kernels on this device may store into a peer's buffer only if the buffer is
+// mapped in this device's context with peer access to its owner
+// (focal_tp_buffer_open does both).  Checked (and peer access enabled) once
+// per pointer and device.
+std::mutex g_peer_mutex;
+struct PeerSeen {
+  const void* ptr;
+  int dev;
+};
+PeerSeen g_peer_seen[256];
+int g_peer_seen_n = 0;
+
+int ensure_peer_access(const void* ptr) {
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lock(g_peer_mutex);
+  for (int i = 0; i < g_peer_seen_n; ++i)
+    if (g_peer_seen[i].ptr == ptr && g_peer_seen[i].dev == dev) return FOCAL_OK;
+  cudaPointerAttributes attr{};
+  rc = check_cuda(cudaPointerGetAttributes(&attr, ptr), "cudaPointerGetAttributes");
+  if (rc) return rc;
+  if (attr.type != cudaMemoryTypeDevice)
+    return set_error(FOCAL_ERR_INVALID_VALUE, "tensor-parallel buffer %p is not device memory", ptr);
+  if (attr.device != dev) {
+    int can = 0;
+    rc = check_cuda(cudaDeviceCanAccessPeer(&can, dev, attr.device), "cudaDeviceCanAccessPeer");
+    if (rc) return rc;
+    if (!can) return set_error(FOCAL_ERR_UNSUPPORTED, "GPU %d cannot access GPU %d's memory", dev, attr.device);
+    const cudaError_t e = cudaDeviceEnablePeerAccess(attr.device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+      (void)cudaGetLastError();  // not an error here; clear it
+    } else {
+      rc = check_cuda(e, "cudaDeviceEnablePeerAccess");
+      if (rc) return rc;
+    }
+  }
+  if (g_peer_seen_n < 256) g_peer_seen[g_peer_seen_n++] = PeerSeen{ptr, dev};
+  return FOCAL_OK;
+}
+
+void forget_peer(const void* ptr) {
+  std::lock_guard<std::mutex> lock(g_peer_mutex);
+  int j = 0;
+  for (int i = 0; i < g_peer_seen_n; ++i)
+    if (g_peer_seen[i].ptr != ptr) g_peer_seen[j++] = g_peer_seen[i];
+  g_peer_seen_n = j;
+}
+
+int tp_params(const focal_tp_comm* comm, int M, int N, TpParams* tp) {
+  if (!comm) return set_error(FOCAL_ERR_INVALID_VALUE, "null tensor-parallel group");
+  if (comm->world < 1 || comm->world > kMaxTp || comm->rank < 0 || comm->rank >= comm->world)
+    return set_error(FOCAL_ERR_INVALID_VALUE, "tensor-parallel group: world %d / rank %d out of range",
+                     comm->world, comm->rank);
+  const size_t need = tp_buffer_bytes(comm->world, M, N);
+  if (comm->bytes < need)
+    return set_error(FOCAL_ERR_WORKSPACE, "tensor-parallel buffers too small: need %zu bytes, have %zu", need,
+                     comm->bytes);
+  *tp = TpParams{};
+  for (int q = 0; q < comm->world; ++q) {
+    if (!comm->peer[q]) return set_error(FOCAL_ERR_INVALID_VALUE, "tensor-parallel buffer of rank %d is null", q);
+    if (!aligned(comm->peer[q], 256))
+      return set_error(FOCAL_ERR_INVALID_VALUE, "tensor-parallel buffers must be 256-byte aligned");
+    if (q != comm->rank) {
+      const int rc = ensure_peer_access(comm->peer[q]);
+      if (rc) return rc;
+    }
+    tp->recv[q] = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(comm->peer[q]) + kTpRecvOffset);
+  }
+  tp->state = static_cast<unsigned int*>(comm->peer[comm->rank]);
+  tp->world = comm->world;
+  tp->rank = comm->rank;
+  return FOCAL_OK;
+}
+
 int run(int epi, const void* x, const int32_t* wq0, const void* s0, const void* z0,
         const int32_t* wq1, const void* s1, const void* z1, void* y, int M, int K, int N,
-        void* workspace, size_t ws_bytes, cudaStream_t stream) {
+        void* workspace, size_t ws_bytes, cudaStream_t stream, const focal_tp_comm* comm = nullptr) {
   clear_error();
   int rc = check_shape(M, K, N);
   if (rc) return rc;
+  TpParams tp{};
+  if (is_tp(epi)) {
+    rc = tp_params(comm, M, N, &tp);
+    if (rc) return rc;
+  }
   const int NW = epi == kEpiSiluMul ? 2 : 1;
   if (!x || !wq0 || !s0 || !z0 || !y || (NW == 2 && (!wq1 || !s1 || !z1)))
     return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
@@ -830,10 +1047,13 @@ int run(int epi, const void* x, const int32_t* wq0, const void* s0, const void* 
   p.RB = N / kRows;
   p.U = (long long)p.TS * p.RB;
   p.sz_tma = sz_tma ? 1 : 0;
+  p.tp = tp;
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* ws = static_cast<uint8_t*>(workspace);
   if (epi == kEpiBf16) return dispatch_mt<1, kEpiBf16>(MT, maps, p, xb, ws, ws_bytes, dev, stream);
   if (epi == kEpiF32) return dispatch_mt<1, kEpiF32>(MT, maps, p, xb, ws, ws_bytes, dev, stream);
+  if (epi == kEpiAllGather) return dispatch_mt<1, kEpiAllGather>(MT, maps, p, xb, ws, ws_bytes, dev, stream);
+  if (epi == kEpiAllReduce) return dispatch_mt<1, kEpiAllReduce>(MT, maps, p, xb, ws, ws_bytes, dev, stream);
   return dispatch_mt<2, kEpiSiluMul>(MT, maps, p, xb, ws, ws_bytes, dev, stream);
 }
 
@@ -885,6 +1105,70 @@ int focal_w4a16_gate_up_silu(const void* x, const int32_t* wq_gate, const void* 
                              size_t ws_bytes, cudaStream_t stream) {
   return gemv::run(gemv::kEpiSiluMul, x, wq_gate, scales_gate, zeros_gate, wq_up, scales_up,
                    zeros_up, h, M, K, N, workspace, ws_bytes, stream);
+}
+
+size_t focal_tp_buffer_size(int world, int max_m, int max_n) {
+  if (world < 1 || world > gemv::kMaxTp || gemv::check_shape(max_m, 256, max_n)) return 0;
+  return gemv::tp_buffer_bytes(world, max_m, max_n);
+}
+
+int focal_tp_buffer_create(size_t bytes, void** buffer, uint8_t* handle) {
+  clear_error();
+  if (!buffer || !handle || bytes == 0) return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer or zero size");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  void* p = nullptr;
+  int rc = check_cuda(cudaMalloc(&p, bytes), "cudaMalloc");
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  rc = check_cuda(cudaMemset(p, 0, bytes), "cudaMemset");
+  if (!rc) rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  if (!rc) rc = check_cuda(cudaIpcGetMemHandle(&h, p), "cudaIpcGetMemHandle");
+  if (rc) {
+    cudaFree(p);
+    return rc;
+  }
+  memcpy(handle, &h, sizeof(h));
+  *buffer = p;
+  return FOCAL_OK;
+}
+
+int focal_tp_buffer_open(const uint8_t* handle, void** peer) {
+  clear_error();
+  if (!handle || !peer) return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const int rc = check_cuda(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  if (rc) return rc;
+  *peer = p;
+  return FOCAL_OK;
+}
+
+int focal_tp_buffer_close(void* peer) {
+  clear_error();
+  if (!peer) return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
+  gemv::forget_peer(peer);
+  return check_cuda(cudaIpcCloseMemHandle(peer), "cudaIpcCloseMemHandle");
+}
+
+int focal_tp_buffer_destroy(void* buffer) {
+  clear_error();
+  if (!buffer) return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
+  return check_cuda(cudaFree(buffer), "cudaFree");
+}
+
+int focal_w4a16_gemv_allgather(const void* x, const int32_t* wq, const void* scales, const void* zeros,
+                               void* y, int M, int K, int N, const focal_tp_comm* comm, void* workspace,
+                               size_t ws_bytes, cudaStream_t stream) {
+  return gemv::run(gemv::kEpiAllGather, x, wq, scales, zeros, nullptr, nullptr, nullptr, y, M, K, N,
+                   workspace, ws_bytes, stream, comm);
+}
+
+int focal_w4a16_gemv_allreduce(const void* x, const int32_t* wq, const void* scales, const void* zeros,
+                               void* y, int M, int K, int N, const focal_tp_comm* comm, void* workspace,
+                               size_t ws_bytes, cudaStream_t stream) {
+  return gemv::run(gemv::kEpiAllReduce, x, wq, scales, zeros, nullptr, nullptr, nullptr, y, M, K, N,
+                   workspace, ws_bytes, stream, comm);
 }
 
 int focal_w4a16_gemv_noalloc(const void* x, const int32_t* wq, const void* scales, const void* zeros,

@@ -18,6 +18,13 @@ The per-rank compute is the sm_100a kernel path (focal_b200.w4a16_linear /
 w4a16_linear_f32 / gqa_decode_attention).  ``local_ops`` lets a caller
 substitute the per-rank compute; the gloo tests use it to check the sharding
 and collectives on CPU.
+
+With a ``TpGroup`` the two W4A16 layers run fused instead: one kernel per
+layer computes the shard and exchanges its row blocks with the other ranks
+over NVLink peer memory (focal_w4a16_gemv_allgather / _allreduce in
+include/focal_b200.h), with no NCCL call on the data path.  The group's
+buffers are created and mapped by the library (CUDA IPC handles, exchanged
+once with ``all_gather_object``).
 """
 from __future__ import annotations
 
@@ -118,22 +125,153 @@ def reduce_partials(partial_f32: torch.Tensor, group=None) -> torch.Tensor:
     return partial_f32.to(torch.bfloat16)
 
 
+# ------------------------------------------------------- fused peer-memory group
+class _DeviceBytes:
+    """A raw device buffer seen as a torch uint8 tensor (zero-copy, through the
+    CUDA array interface)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class TpGroup:
+    """Peer-memory buffers of a tensor-parallel group for the fused linears.
+
+    Each rank creates one zero-filled buffer of
+    ``focal_tp_buffer_size(world, max_m, max_n)`` bytes on its GPU
+    (focal_tp_buffer_create), sends its CUDA IPC handle to the other ranks
+    (``all_gather_object``), and maps theirs for its own GPU
+    (focal_tp_buffer_open).  Every rank must make the same sequence of fused
+    calls with the same shapes, on one stream per rank (the buffers hold
+    per-call state), and each rank needs its own GPU.  ``world == 1`` (no
+    process group) runs the same kernels against the local buffer alone.
+    """
+
+    def __init__(self, max_m: int = 8, max_n: int = 65536, group=None, device=None):
+        import ctypes
+
+        from . import _lib
+
+        self.group = group
+        self.world = world_size(group)
+        self.rank = rank_of(group)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        L = _lib.lib()
+        self.bytes = int(L.focal_tp_buffer_size(self.world, max_m, max_n))
+        if self.bytes == 0:
+            raise ValueError(f"no tensor-parallel buffer for world={self.world} M<={max_m} N<={max_n}")
+        if self.world > 1:
+            # ranks whose kernels wait on one another must not share a GPU
+            uuids = [None] * self.world
+            dist.all_gather_object(uuids, str(torch.cuda.get_device_properties(self.device).uuid), group=group)
+            if len(set(uuids)) != self.world:
+                raise ValueError(f"tensor-parallel ranks share a GPU ({uuids}); every rank needs its own")
+        handle = (ctypes.c_uint8 * 64)()
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.call("focal_tp_buffer_create", self.bytes, ctypes.byref(ptr), handle)
+            self._own = ptr.value
+            self._opened = []
+            peers = [0] * self.world
+            peers[self.rank] = self._own
+            if self.world > 1:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, bytes(handle), group=group)
+                for q in range(self.world):
+                    if q != self.rank:
+                        p = ctypes.c_void_p()
+                        _lib.call("focal_tp_buffer_open", (ctypes.c_uint8 * 64).from_buffer_copy(handles[q]),
+                                  ctypes.byref(p))
+                        peers[q] = p.value
+                        self._opened.append(p.value)
+                dist.barrier(group=group)  # every buffer is zero and mapped before any rank stores into it
+        # this rank's buffer as a tensor: [0:4] completed calls, [4:8] CTAs done
+        self.buf = torch.as_tensor(_DeviceBytes(self._own, self.bytes), device=self.device)
+        self.comm = _lib.TpComm()
+        for q, p in enumerate(peers):
+            self.comm.peer[q] = p
+        self.comm.bytes = self.bytes
+        self.comm.world = self.world
+        self.comm.rank = self.rank
+        self._ws = None
+        self._ws_bytes = 0
+
+    def _workspace(self, M, K, N):
+        from . import _lib
+
+        need = int(_lib.lib().focal_w4a16_workspace_size(M, K, N))
+        if need > self._ws_bytes:
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+            self._ws_bytes = need
+        return self._ws
+
+    def _call(self, name, x, wq, scales, zeros, y):
+        import ctypes
+
+        from . import _lib
+
+        M, K = x.shape
+        N = wq.shape[0]
+        ws = self._workspace(M, K, N)
+        _lib.call(name, x.data_ptr(), wq.data_ptr(), scales.data_ptr(), zeros.data_ptr(), y.data_ptr(), M, K, N,
+                  ctypes.byref(self.comm), ws.data_ptr(), self._ws_bytes,
+                  torch.cuda.current_stream(self.device).cuda_stream)
+        return y
+
+    def allgather_linear(self, x, wq, scales, zeros) -> torch.Tensor:
+        """Column-parallel shard + all-gather in one kernel: y [M, world*N] bf16."""
+        M, N = x.shape[0], wq.shape[0]
+        y = torch.empty((M, self.world * N), dtype=torch.bfloat16, device=x.device)
+        return self._call("focal_w4a16_gemv_allgather", x, wq, scales, zeros, y)
+
+    def allreduce_linear(self, x_local, wq, scales, zeros) -> torch.Tensor:
+        """Row-parallel shard + fp32 all-reduce in one kernel: y [M, N] bf16."""
+        M, N = x_local.shape[0], wq.shape[0]
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=x_local.device)
+        return self._call("focal_w4a16_gemv_allreduce", x_local, wq, scales, zeros, y)
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's, once every rank is
+        done with the group (collective over the group's ranks)."""
+        from . import _lib
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no rank stores into a buffer after this
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                _lib.call("focal_tp_buffer_close", p)
+            self._opened = []
+            if self.world > 1:
+                dist.barrier(group=self.group)  # every mapping of this rank's buffer is gone
+            self.buf = None
+            _lib.call("focal_tp_buffer_destroy", self._own)
+        self._own = None
+
+
 # ---------------------------------------------------------------------- layers
 class ColumnParallelW4A16:
     """y = x W^T with W sharded over N; returns the full bf16 y on every rank."""
 
-    def __init__(self, wq, scales, zeros, group=None, ops: LocalOps | None = None, gather=True):
+    def __init__(self, wq, scales, zeros, group=None, ops: LocalOps | None = None, gather=True,
+                 fused: TpGroup | None = None):
         self.group = group
         self.rank = rank_of(group)
         self.world = world_size(group)
         self.shard = column_shard(wq, scales, zeros, self.rank, self.world)
         self.ops = ops or cuda_ops()
         self.gather = gather
+        self.fused = fused
 
     def local(self, x):
         return self.ops.linear_bf16(x, *self.shard)
 
     def __call__(self, x):
+        if self.fused is not None and self.gather:
+            return self.fused.allgather_linear(x, *self.shard)
         y = self.local(x)
         return gather_columns(y, self.group) if self.gather else y
 
@@ -141,17 +279,21 @@ class ColumnParallelW4A16:
 class RowParallelW4A16:
     """y = x W^T with W (and x) sharded over K; fp32 all-reduce, one bf16 rounding."""
 
-    def __init__(self, wq, scales, zeros, group=None, ops: LocalOps | None = None):
+    def __init__(self, wq, scales, zeros, group=None, ops: LocalOps | None = None,
+                 fused: TpGroup | None = None):
         self.group = group
         self.rank = rank_of(group)
         self.world = world_size(group)
         self.shard = row_shard(wq, scales, zeros, self.rank, self.world)
         self.ops = ops or cuda_ops()
+        self.fused = fused
 
     def local(self, x_local):
         return self.ops.linear_f32(x_local, *self.shard)
 
     def __call__(self, x_local):
+        if self.fused is not None:
+            return self.fused.allreduce_linear(x_local, *self.shard)
         return reduce_partials(self.local(x_local), self.group)
 
 

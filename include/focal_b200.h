@@ -108,6 +108,72 @@ int focal_w4a16_gate_up_silu(const void* x, const int32_t* wq_gate, const void* 
                              const void* zeros_up, void* h, int M, int K, int N, void* workspace,
                              size_t ws_bytes, cudaStream_t stream);
 
+/* ---------------------------------------- tensor-parallel fused linears ---
+ * New entry points (the reference has no multi-GPU code): the linear layer
+ * with its collective in the same kernel.  Each 64-row block, once finished,
+ * is stored into every other rank's buffer over NVLink peer memory, every
+ * value in one 64-bit store together with the call's epoch, and completed
+ * once the same block's words from every rank have arrived (a bounded poll of
+ * the epochs; no fences or separate flags).  No TMA or library kernel touches
+ * peer memory, and nothing uses multicast.
+ *
+ * The group: one buffer per rank, all of focal_tp_buffer_size() bytes or more,
+ * zero-filled before the first call, 256-byte aligned, and mapped into every
+ * rank's process for its own device (peer[q] is rank q's buffer as seen
+ * here, peer[rank] the local one; focal_tp_buffer_create / _open below make
+ * and map them).  Every rank must make the same sequence
+ * of fused calls on its group, with the same M and N, each rank on its own
+ * GPU; all CTAs of a call wait for the other ranks' blocks, so a rank that
+ * does not make the call makes the others give up after about a second and
+ * set focal_device_status to 2 (the group must then be rebuilt: zero the
+ * buffers on every rank).  Calls on one group must be ordered on one stream
+ * per rank; the buffers hold per-call state, so a group serves one stream. */
+typedef struct focal_tp_comm {
+  void* peer[8];  /* rank q's buffer as mapped in this process            */
+  size_t bytes;   /* usable bytes of each buffer (the smallest of them)   */
+  int world;      /* ranks, 1..8                                           */
+  int rank;       /* this process's rank                                   */
+} focal_tp_comm;
+
+/* Bytes of each rank's buffer for fused calls with M <= max_m, N <= max_n
+ * (per-rank N); 0 if world or the shape is outside the contract. */
+size_t focal_tp_buffer_size(int world, int max_m, int max_n);
+
+/* This rank's buffer: cudaMalloc'd on the current device, zero-filled (the
+ * call waits for the fill), and exported as a 64-byte CUDA IPC handle
+ * (`handle`) to send to every other rank. */
+int focal_tp_buffer_create(size_t bytes, void** buffer, uint8_t* handle);
+
+/* Maps another rank's buffer, given its handle, for kernels on the current
+ * device (which must be this rank's GPU), enabling peer access as needed.
+ * A mapping made in another device's context (for instance by a framework
+ * that opens the handle on its owner's device) is not usable by the fused
+ * kernels on this device. */
+int focal_tp_buffer_open(const uint8_t* handle, void** peer);
+
+/* Unmaps a buffer opened with focal_tp_buffer_open. */
+int focal_tp_buffer_close(void* peer);
+
+/* Frees this rank's buffer, once no rank uses it any more. */
+int focal_tp_buffer_destroy(void* buffer);
+
+/* Column-parallel linear + all-gather: this rank holds rows
+ * [rank*N, (rank+1)*N) of a [world*N, K] weight (wq [N, K/8], scales and
+ * zeros [N, K/128]) and the full x [M, K]; y is bf16 [M, world*N], every
+ * rank's block in its columns, identical on every rank. */
+int focal_w4a16_gemv_allgather(const void* x, const int32_t* wq, const void* scales, const void* zeros,
+                               void* y, int M, int K, int N, const focal_tp_comm* comm, void* workspace,
+                               size_t ws_bytes, cudaStream_t stream);
+
+/* Row-parallel linear + all-reduce: this rank holds K columns
+ * [rank*K, (rank+1)*K) of a [N, world*K] weight (wq [N, K/8], scales and
+ * zeros [N, K/128]) and the matching x slice [M, K]; y is bf16 [M, N] =
+ * bf16(sum over ranks, in rank order, of the fp32 partial products),
+ * bit-identical on every rank. */
+int focal_w4a16_gemv_allreduce(const void* x, const int32_t* wq, const void* scales, const void* zeros,
+                               void* y, int M, int K, int N, const focal_tp_comm* comm, void* workspace,
+                               size_t ws_bytes, cudaStream_t stream);
+
 /* fp32 [N, K] dequantized weights, bit-identical to dequant_ref
  * (focal_w4a16/__init__.py:57-91); exposes the kernels' int4 unpacking. */
 int focal_w4a16_dequant(const int32_t* wq, const void* scales, const void* zeros, float* w,

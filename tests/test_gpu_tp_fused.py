@@ -1,0 +1,86 @@
+"""The fused tensor-parallel linears (focal_w4a16_gemv_allgather / _allreduce),
+called through the C ABI.
+
+One GPU: a group of one rank runs the same kernels (stores into its own
+buffer, releases and waits on its own flags); the outputs must equal the plain
+linear's bit for bit, over repeated calls that alternate the two receive
+halves and change shape.  Two or more GPUs: tests/tp_fused_worker.py under
+torchrun checks, on every rank, that the fused all-gather equals the NCCL
+all-gather of the plain shards and that the fused all-reduce equals the rank-
+order fp32 sum of the plain fp32 partials, both bit for bit, and both against
+the oracle within the linear's tolerance.
+"""
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import w4a16 as ow
+from tests import _capi as C
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def test_single_rank_group_matches_plain_linear(cuda):
+    from focal_b200 import _lib
+    from focal_b200.tp import TpGroup
+
+    group = TpGroup(max_m=8, max_n=8192, device=cuda)
+    cases = [(8, 4096, 8192), (1, 8192, 4096), (4, 4096, 4096), (8, 11008, 4096), (2, 1024, 192)]
+    for it in range(3):
+        for i, (M, K, N) in enumerate(cases):
+            x, wq, s, z = (C.to_dev_bf16(a, cuda) if j == 0 else C.to_dev(a, cuda)
+                           for j, a in enumerate(ow.baseline_case(M, K, N, seed=300 + 10 * i + it)))
+            plain = C.gemv(x, wq, s, z)
+            ag = group.allgather_linear(x, wq, s, z)
+            ar = group.allreduce_linear(x, wq, s, z)
+            assert torch.equal(ag.view(torch.int16), plain.view(torch.int16)), (M, K, N, it)
+            assert torch.equal(ar.view(torch.int16), plain.view(torch.int16)), (M, K, N, it)
+    torch.cuda.synchronize()
+    status = __import__("ctypes").c_int(-1)
+    assert _lib.lib().focal_device_status(status) == 0 and status.value == 0
+    # two kernels per case and iteration advanced the group's epoch
+    state = group.buf[:8].view(torch.int32).cpu().tolist()
+    assert state == [2 * 3 * len(cases), 0]
+    group.close()
+
+
+def test_group_rejects_bad_arguments(cuda):
+    import ctypes
+
+    from focal_b200 import _lib
+    from focal_b200.tp import TpGroup
+
+    group = TpGroup(max_m=8, max_n=512, device=cuda)
+    x, wq, s, z = (C.to_dev_bf16(a, cuda) if j == 0 else C.to_dev(a, cuda)
+                   for j, a in enumerate(ow.baseline_case(8, 1024, 1024, seed=1)))
+    y = torch.empty((8, 1024), dtype=torch.bfloat16, device=cuda)
+    ws, n = C.w4a16_workspace(8, 1024, 1024, cuda)
+    L = _lib.lib()
+    rc = L.focal_w4a16_gemv_allreduce(x.data_ptr(), wq.data_ptr(), s.data_ptr(), z.data_ptr(), y.data_ptr(),
+                                      8, 1024, 1024, ctypes.byref(group.comm), ws.data_ptr(), n, C.stream_ptr())
+    assert rc == _lib.FOCAL_ERR_WORKSPACE and "tensor-parallel buffers too small" in _lib.last_error()
+    bad = _lib.TpComm()
+    bad.world, bad.rank, bad.bytes = 2, 2, group.bytes
+    rc = L.focal_w4a16_gemv_allgather(x.data_ptr(), wq.data_ptr(), s.data_ptr(), z.data_ptr(), y.data_ptr(),
+                                      8, 1024, 512, ctypes.byref(bad), ws.data_ptr(), n, C.stream_ptr())
+    assert rc == _lib.FOCAL_ERR_INVALID_VALUE and "out of range" in _lib.last_error()
+    group.close()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_group_over_nvlink():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=str(ROOT))
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29531",
+           str(ROOT / "tests" / "tp_fused_worker.py")]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)
+    errors = [ln for ln in r.stderr.splitlines() if "rror" in ln or "rank" in ln][:40]
+    assert r.returncode == 0, r.stdout[-3000:] + "\n".join(errors)
+    assert r.stdout.count("tp fused ok") == 2, r.stdout[-4000:]

@@ -80,3 +80,24 @@ def test_status_codes_have_messages_without_gpu():
     with pytest.raises(_lib.FocalError, match="unsupported M"):
         _lib.call("focal_w4a16_check_shape", 16, 4096, 4096)
     assert isinstance(ctypes.c_int(0).value, int)
+
+
+def test_tp_buffer_sizing_and_argument_errors():
+    L = _lib.lib()
+    one = L.focal_tp_buffer_size(1, 8, 4096)
+    two = L.focal_tp_buffer_size(2, 8, 4096)
+    # 256 B of state, then two receive halves of world x M x N 8-byte
+    # {payload, epoch} words
+    assert one == 256 + 2 * 1 * 8 * 4096 * 8
+    assert two - one == 2 * 8 * 4096 * 8
+    assert L.focal_tp_buffer_size(9, 8, 4096) == 0
+    assert L.focal_tp_buffer_size(2, 9, 4096) == 0
+    assert L.focal_tp_buffer_size(2, 8, 100) == 0
+    for name in ("focal_w4a16_gemv_allgather", "focal_w4a16_gemv_allreduce"):
+        rc = getattr(L, name)(None, None, None, None, None, 8, 4096, 4096, None, None, 0, None)
+        assert rc == _lib.FOCAL_ERR_INVALID_VALUE and "null tensor-parallel group" in _lib.last_error()
+    comm = _lib.TpComm()
+    comm.world, comm.rank, comm.bytes = 2, 1, two
+    rc = L.focal_w4a16_gemv_allreduce(None, None, None, None, None, 8, 4096, 4096, ctypes.byref(comm),
+                                      None, 0, None)
+    assert rc == _lib.FOCAL_ERR_INVALID_VALUE and "rank 0 is null" in _lib.last_error()
