@@ -69,7 +69,7 @@ constexpr int kThreads = 32 * (kConsumerWarps + kPairs);
 // 8 x 16 KB) of weights in flight.
 __host__ __device__ constexpr int ring_of(int NW) { return NW == 1 ? 3 : 2; }
 constexpr int kMaxCtasPerSm = 4;        // bound on unit ranges per SM, used to size the workspace
-constexpr int kSumBatch = 8;            // partial sums loaded together by a finishing CTA
+constexpr int kSumBatch = 8;            // partial-sum ranges loaded together by a finisher (MT * NW <= 2)
 constexpr int kMinUnitsPerRange = 4;    // below this, fewer ranges beat more split overhead
 // Scale/zero quad slots per sub-pipeline when they arrive by TMA: the slot of
 // quad k is refilled for quad k + 2, whose first unit is issued only after the
@@ -232,101 +232,110 @@ __device__ __forceinline__ void store_out(void* y, size_t yi, const float (&v)[N
 
 // Output of finished row block rb, written by the 64 threads of the pair that
 // finished it: thread ptid owns row ptid of the block for every token, and
-// value(tok, row, v) yields the block's fp32 sums.  The tensor-parallel
-// epilogues first send the thread's elements to every other rank as
-// {payload, epoch} words (64-bit relaxed stores at system scope, over NVLink
-// for peers), keeping its own in registers, then poll (bounded) the words the
-// other ranks sent for the same elements.  All-gather writes each rank's bf16
-// block into its columns of y [M, N * world]; all-reduce adds the ranks' fp32
-// values in rank order (the same order on every rank, so all ranks get the
-// same bits) and rounds once to bf16.
-template <int MT, int EPI, int NW, class ValueFn>
-__device__ __forceinline__ void finish_block(const Params& p, int rb, int ptid, unsigned int e, ValueFn&& value) {
+// values(v) yields the block's fp32 sums of that row, v[token][matrix], for
+// all tokens at once (tokens >= M are ignored).  The tensor-parallel
+// epilogues only send here: each element goes to every rank (this one
+// included) as a {payload, epoch} word, by a 64-bit relaxed store at system
+// scope (over NVLink for peers); tp_complete writes y later.
+template <int MT, int EPI, int NW, class ValuesFn>
+__device__ __forceinline__ void finish_block(const Params& p, int rb, int ptid, unsigned int e, ValuesFn&& values) {
   const size_t col = (size_t)rb * kRows + ptid;
+  float v[MT][NW];
+  values(v);
   if constexpr (!is_tp(EPI)) {
-    for (int tok = 0; tok < p.M; ++tok) {
-      float v[NW];
-      value(tok, ptid, v);
-      store_out<EPI, NW>(p.y, (size_t)tok * p.N + col, v);
-    }
+#pragma unroll
+    for (int tok = 0; tok < MT; ++tok)
+      if (tok < p.M) store_out<EPI, NW>(p.y, (size_t)tok * p.N + col, v[tok]);
   } else {
     static_assert(NW == 1, "tensor-parallel epilogues take one weight matrix");
-    float mine[MT];
     unsigned long long word[MT];
 #pragma unroll
     for (int i = 0; i < MT; ++i) {
-      mine[i] = 0.f;
-      if (i < p.M) {
-        float v[1];
-        value(i, ptid, v);
-        mine[i] = EPI == kEpiAllGather ? __bfloat162float(__float2bfloat16_rn(v[0])) : v[0];
-      }
       const unsigned int payload = EPI == kEpiAllGather
-                                       ? (unsigned int)__bfloat16_as_ushort(__float2bfloat16_rn(mine[i]))
-                                       : __float_as_uint(mine[i]);
+                                       ? (unsigned int)__bfloat16_as_ushort(__float2bfloat16_rn(v[i][0]))
+                                       : __float_as_uint(v[i][0]);
       word[i] = ((unsigned long long)e << 32) | payload;
     }
     const size_t slab = (size_t)p.M * p.N;  // words per (half, source rank)
-    const size_t half = (size_t)(e & 1u) * p.tp.world * slab;
+    const size_t at = (size_t)(e & 1u) * p.tp.world * slab + (size_t)p.tp.rank * slab + col;
 #pragma unroll
     for (int q = 0; q < kMaxTp; ++q) {
-      if (q < p.tp.world && q != p.tp.rank) {
-        unsigned long long* dst = p.tp.recv[q] + half + (size_t)p.tp.rank * slab + col;
+      if (q < p.tp.world) {
 #pragma unroll
         for (int i = 0; i < MT; ++i)
-          if (i < p.M) st_relaxed_sys_u64(dst + (size_t)i * p.N, word[i]);
+          if (i < p.M) st_relaxed_sys_u64(p.tp.recv[q] + at + (size_t)i * p.N, word[i]);
       }
     }
-    const unsigned long long* here = p.tp.recv[p.tp.rank] + half + col;
-    float acc[MT];
-    bool timed_out = false;
-    for (int src = 0; src < p.tp.world; ++src) {
-      float val[MT];
-      if (src == p.tp.rank) {
+  }
+}
+
+// Completion of a row block this pair finished and sent: thread ptid polls
+// (bounded) the words every rank sent for row ptid of block rb until their
+// epochs read e, then writes y.  All-gather stores each rank's bf16 block in
+// its columns of y [M, N * world]; all-reduce adds the ranks' fp32 values in
+// rank order (the same on every rank, so all ranks get the same bits) and
+// rounds once to bf16.  The pair completes a block only at its next finish or
+// at the end of its range, so the exchange's NVLink latency overlaps the
+// pair's remaining units.
+template <int MT, int EPI>
+__device__ __forceinline__ void tp_complete(const Params& p, int rb, int ptid, unsigned int e) {
+  constexpr int S = MT >= 8 ? 2 : MT >= 4 ? 4 : 8;  // source ranks polled together
+  const size_t col = (size_t)rb * kRows + ptid;
+  const size_t slab = (size_t)p.M * p.N;
+  const unsigned long long* here = p.tp.recv[p.tp.rank] + (size_t)(e & 1u) * p.tp.world * slab + col;
+  const unsigned long long ready_word = (unsigned long long)e << 32;
+  float acc[MT];
 #pragma unroll
-        for (int i = 0; i < MT; ++i) val[i] = mine[i];
-      } else {
-        const unsigned long long* r = here + (size_t)src * slab;
-        unsigned long long w[MT];
+  for (int i = 0; i < MT; ++i) acc[i] = 0.f;
+  for (int s0 = 0; s0 < p.tp.world; s0 += S) {
+    unsigned long long w[S][MT];
 #pragma unroll
-        for (int i = 0; i < MT; ++i) w[i] = i < p.M ? ld_relaxed_sys_u64(r + (size_t)i * p.N) : word[i];
-        const long long t0 = clock64();
-        while (!timed_out) {
-          bool ready = true;
-#pragma unroll
-          for (int i = 0; i < MT; ++i) ready = ready && (unsigned int)(w[i] >> 32) == e;
-          if (ready) break;
-          if (clock64() - t0 > kWaitLimitCycles) {
-            timed_out = true;  // the rest of this block is skipped: its output is garbage
-            atomicExch(p.status, kDevPeerTimeout);
-            break;
-          }
-#pragma unroll
-          for (int i = 0; i < MT; ++i)
-            if ((unsigned int)(w[i] >> 32) != e) w[i] = ld_relaxed_sys_u64(r + (size_t)i * p.N);
-        }
-#pragma unroll
-        for (int i = 0; i < MT; ++i)
-          val[i] = EPI == kEpiAllGather
-                       ? __bfloat162float(__ushort_as_bfloat16((unsigned short)(w[i] & 0xFFFFu)))
-                       : __uint_as_float((unsigned int)w[i]);
-      }
-      if (EPI == kEpiAllGather) {
-#pragma unroll
-        for (int i = 0; i < MT; ++i)
-          if (i < p.M)
-            static_cast<__nv_bfloat16*>(p.y)[((size_t)i * p.tp.world + src) * p.N + col] =
-                __float2bfloat16_rn(val[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < MT; ++i) acc[i] = src == 0 ? val[i] : acc[i] + val[i];
-      }
-    }
-    if (EPI == kEpiAllReduce) {
+    for (int j = 0; j < S; ++j)
 #pragma unroll
       for (int i = 0; i < MT; ++i)
-        if (i < p.M) static_cast<__nv_bfloat16*>(p.y)[(size_t)i * p.N + col] = __float2bfloat16_rn(acc[i]);
+        w[j][i] = (s0 + j < p.tp.world && i < p.M) ? ld_relaxed_sys_u64(here + (size_t)(s0 + j) * slab + (size_t)i * p.N)
+                                                  : ready_word;
+    const long long t0 = clock64();
+    while (true) {
+      bool ready = true;
+#pragma unroll
+      for (int j = 0; j < S; ++j)
+#pragma unroll
+        for (int i = 0; i < MT; ++i) ready = ready && (unsigned int)(w[j][i] >> 32) == e;
+      if (ready) break;
+      if (clock64() - t0 > kWaitLimitCycles) {
+        atomicExch(p.status, kDevPeerTimeout);  // this block's output is garbage
+        break;
+      }
+#pragma unroll
+      for (int j = 0; j < S; ++j)
+#pragma unroll
+        for (int i = 0; i < MT; ++i)
+          if ((unsigned int)(w[j][i] >> 32) != e)
+            w[j][i] = ld_relaxed_sys_u64(here + (size_t)(s0 + j) * slab + (size_t)i * p.N);
     }
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+      const int src = s0 + j;
+      if (src < p.tp.world) {
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+          if (EPI == kEpiAllGather) {
+            if (i < p.M)
+              reinterpret_cast<unsigned short*>(p.y)[((size_t)i * p.tp.world + src) * p.N + col] =
+                  (unsigned short)(w[j][i] & 0xFFFFu);
+          } else {
+            const float val = __uint_as_float((unsigned int)w[j][i]);
+            acc[i] = src == 0 ? val : acc[i] + val;
+          }
+        }
+      }
+    }
+  }
+  if (EPI == kEpiAllReduce) {
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+      if (i < p.M) static_cast<__nv_bfloat16*>(p.y)[(size_t)i * p.N + col] = __float2bfloat16_rn(acc[i]);
   }
 }
 
@@ -548,6 +557,13 @@ __global__ void __maxnreg__(160)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[mat][tl][j] = 0.f;
 
+    int pend_rb = -1;  // tensor-parallel: a row block this pair sent but has not completed
+    auto finished = [&](int frb) {
+      if constexpr (is_tp(EPI)) {
+        if (pend_rb >= 0) tp_complete<MT, EPI>(p, pend_rb, ptid, tp_e);
+        pend_rb = frb;
+      }
+    };
     int rb = rb0, st = st0, qs = kSzQuadSlots - 1;
     for (int j = 0; j < nu; ++j) {
       const bool oq = (j == 0) || ((st & 3) == 0);
@@ -658,10 +674,13 @@ __global__ void __maxnreg__(160)
         const int nout = p.M * kRows;
         if (u0 <= rb_lo && u1 >= rb_hi) {
           // the whole row block was this range's
-          finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](int tok, int row, float(&v)[NW]) {
+          finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](float(&v)[MT][NW]) {
 #pragma unroll
-            for (int mat = 0; mat < NW; ++mat) v[mat] = red[(mat * MT + tok) * kRows + row];
+            for (int tok = 0; tok < MT; ++tok)
+#pragma unroll
+              for (int mat = 0; mat < NW; ++mat) v[tok][mat] = red[(mat * MT + tok) * kRows + ptid];
           });
+          finished(rb);
         } else if (4 * (int)blockIdx.x + 3 < p.P && rb_lo == unit_begin(4 * blockIdx.x, p.U, p.P) &&
                    rb_hi == unit_begin(4 * blockIdx.x + 4, p.U, p.P)) {
           // This CTA's four ranges are exactly this row block (so each pair has
@@ -673,15 +692,19 @@ __global__ void __maxnreg__(160)
           if (ptid == 0) *flag = (atom_add_acq_rel_cta_shared(base + L.flag + 16, 1u) == kPairs - 1);
           named_barrier(bar, 64);
           if (*flag) {
-            finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](int tok, int row, float(&v)[NW]) {
+            finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](float(&v)[MT][NW]) {
 #pragma unroll
-              for (int mat = 0; mat < NW; ++mat) {
-                v[mat] = 0.f;
+              for (int tok = 0; tok < MT; ++tok)
 #pragma unroll
-                for (int q = 0; q < kPairs; ++q)
-                  v[mat] += reinterpret_cast<const float*>(sm + L.red)[((q * NW + mat) * MT + tok) * kRows + row];
-              }
+                for (int mat = 0; mat < NW; ++mat) {
+                  v[tok][mat] = 0.f;
+#pragma unroll
+                  for (int q = 0; q < kPairs; ++q)
+                    v[tok][mat] +=
+                        reinterpret_cast<const float*>(sm + L.red)[((q * NW + mat) * MT + tok) * kRows + ptid];
+                }
             });
+            finished(rb);
           }
         } else {
           // publish this range's partial; the last of the row block's ranges finishes it
@@ -708,28 +731,38 @@ __global__ void __maxnreg__(160)
             // Partial slots: a range after c_first began inside this row block
             // (slot 2c); c_first used slot 2c + 1 unless it began exactly at rb_lo.
             const long long first_slot = 2LL * c_first + (unit_begin(c_first, p.U, p.P) == rb_lo ? 0 : 1);
-            finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](int tok, int row, float(&v)[NW]) {
+            finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](float(&v)[MT][NW]) {
+              // every token's partials of kB ranges loaded together (one L2
+              // round trip per batch), added in range order (deterministic)
+              constexpr int kB = MT * NW >= 8 ? 2 : MT * NW >= 4 ? 4 : kSumBatch;
 #pragma unroll
-              for (int mat = 0; mat < NW; ++mat) v[mat] = 0.f;
-              // fixed order (deterministic sums); loads issued a batch at a time
-              for (int cb = c_first; cb <= c_last; cb += kSumBatch) {
-                float part[kSumBatch][NW];
+              for (int tok = 0; tok < MT; ++tok)
 #pragma unroll
-                for (int e = 0; e < kSumBatch; ++e) {
+                for (int mat = 0; mat < NW; ++mat) v[tok][mat] = 0.f;
+              for (int cb = c_first; cb <= c_last; cb += kB) {
+                float part[kB][MT][NW];
+#pragma unroll
+                for (int e = 0; e < kB; ++e) {
                   const int c = cb + e;
                   const long long ps = c == c_first ? first_slot : 2LL * (c <= c_last ? c : cb);
-                  const float* src = p.partials + ps * slot_floats(MT, NW);
+                  const float* src = p.partials + ps * slot_floats(MT, NW) + ptid;
 #pragma unroll
-                  for (int mat = 0; mat < NW; ++mat)
-                    part[e][mat] = c <= c_last ? __ldcg(src + (mat * MT + tok) * kRows + row) : 0.f;
+                  for (int tok = 0; tok < MT; ++tok)
+#pragma unroll
+                    for (int mat = 0; mat < NW; ++mat)
+                      part[e][tok][mat] =
+                          (c <= c_last && tok < p.M) ? __ldcg(src + (mat * MT + tok) * kRows) : 0.f;
                 }
 #pragma unroll
-                for (int e = 0; e < kSumBatch; ++e)
+                for (int e = 0; e < kB; ++e)
 #pragma unroll
-                  for (int mat = 0; mat < NW; ++mat) v[mat] += part[e][mat];
+                  for (int tok = 0; tok < MT; ++tok)
+#pragma unroll
+                    for (int mat = 0; mat < NW; ++mat) v[tok][mat] += part[e][tok][mat];
               }
             });
             if (ptid == 0) p.counters[rb] = 0u;
+            finished(rb);
           }
         }
         named_barrier(bar, 64);  // red and the flag are rewritten by the next run
@@ -739,13 +772,18 @@ __global__ void __maxnreg__(160)
         ++rb;
       }
     }
+    if constexpr (is_tp(EPI)) {
+      if (pend_rb >= 0) tp_complete<MT, EPI>(p, pend_rb, ptid, tp_e);
+    }
   }
 
   if (!ok && p.status) atomicExch(p.status, kDevWaitTimeout);
   if constexpr (is_tp(EPI)) {
     // the last CTA to finish advances this rank's epoch for the next call
     __syncthreads();
-    if (threadIdx.x == 0 && atom_add_acq_rel_gpu(p.tp.state + 1, 1u) == gridDim.x - 1) {
+    // (relaxed: the count publishes nothing; the next call reads the state
+    // only after this grid has completed)
+    if (threadIdx.x == 0 && atomicAdd(p.tp.state + 1, 1u) == gridDim.x - 1) {
       p.tp.state[1] = 0u;
       p.tp.state[0] = tp_e;
     }

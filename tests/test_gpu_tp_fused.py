@@ -84,3 +84,42 @@ def test_two_rank_group_over_nvlink():
     errors = [ln for ln in r.stderr.splitlines() if "rror" in ln or "rank" in ln][:40]
     assert r.returncode == 0, r.stdout[-3000:] + "\n".join(errors)
     assert r.stdout.count("tp fused ok") == 2, r.stdout[-4000:]
+
+
+def test_missing_peer_times_out_with_status(cuda):
+    """A two-rank group whose second buffer nobody ever writes (one GPU, one
+    kernel, a word that nothing sets): every bounded poll gives up after about
+    a second, the call's device status reads 2 (peer timeout), and the context
+    stays usable for later calls."""
+    import ctypes
+    import time
+
+    from focal_b200 import _lib
+
+    L = _lib.lib()
+    M, K, N = 1, 1024, 256
+    nbytes = int(L.focal_tp_buffer_size(2, M, N))
+    bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=cuda) for _ in range(2)]
+    comm = _lib.TpComm()
+    comm.peer[0], comm.peer[1] = bufs[0].data_ptr(), bufs[1].data_ptr()
+    comm.bytes, comm.world, comm.rank = nbytes, 2, 0
+    x, wq, s, z = (C.to_dev_bf16(a, cuda) if j == 0 else C.to_dev(a, cuda)
+                   for j, a in enumerate(ow.baseline_case(M, K, N, seed=5)))
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
+    ws, n = C.w4a16_workspace(M, K, N, cuda)
+    assert L.focal_reset_device_status() == 0
+    t0 = time.perf_counter()
+    rc = L.focal_w4a16_gemv_allreduce(x.data_ptr(), wq.data_ptr(), s.data_ptr(), z.data_ptr(), y.data_ptr(),
+                                      M, K, N, ctypes.byref(comm), ws.data_ptr(), n, C.stream_ptr())
+    assert rc == 0
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    status = ctypes.c_int(-1)
+    assert L.focal_device_status(status) == 0 and status.value == 2, status.value
+    assert 0.3 < waited < 30, waited
+    assert L.focal_reset_device_status() == 0
+    # the context still works: a plain call matches the oracle
+    assert_close = ow.allclose_report(C.bf16_bits(C.gemv(x, wq, s, z)), ow.linear(*ow.baseline_case(M, K, N, seed=5)),
+                                      2e-2, 1e-2)
+    assert assert_close["allclose"], assert_close
+    assert L.focal_device_status(status) == 0 and status.value == 0
