@@ -72,6 +72,30 @@ def decode_mlp(x, gate, up, down) -> torch.Tensor:
     return w4a16_linear(w4a16_gate_up_silu(x, gate, up), *down)
 
 
+def w4a16_tile_pack(wq: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor) -> torch.Tensor:
+    """Offline re-layout of (wq, scales, zeros) into unit-tiled weights: a flat
+    uint8 tensor, one contiguous 8704-byte chunk per 64 rows x 256 K values
+    (include/focal_b200.h).  The linears below give the same bits on it as
+    their reference-layout counterparts on the original weights."""
+    return _ext().tile_pack(wq, scales, zeros)
+
+
+def w4a16_linear_tiled(x: torch.Tensor, tiles: torch.Tensor, N: int) -> torch.Tensor:
+    """w4a16_linear on unit-tiled weights (N output rows)."""
+    return _ext().w4a16_linear_tiled(x, tiles, N)
+
+
+def w4a16_linear_tiled_f32(x: torch.Tensor, tiles: torch.Tensor, N: int) -> torch.Tensor:
+    """w4a16_linear_f32 on unit-tiled weights."""
+    return _ext().w4a16_linear_tiled_f32(x, tiles, N)
+
+
+def w4a16_gate_up_silu_tiled(x: torch.Tensor, tiles_gate: torch.Tensor, tiles_up: torch.Tensor,
+                             N: int) -> torch.Tensor:
+    """w4a16_gate_up_silu on unit-tiled gate and up weights."""
+    return _ext().w4a16_gate_up_silu_tiled(x, tiles_gate, tiles_up, N)
+
+
 def check_shape(M: int, K: int, N: int) -> None:
     """Raise RuntimeError (reference wording) if (M, K, N) is outside the contract."""
     from . import _lib

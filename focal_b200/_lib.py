@@ -43,6 +43,12 @@ SIGNATURES = {
     "focal_w4a16_gemv_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "focal_w4a16_gemv_f32": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
     "focal_w4a16_gate_up_silu": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
+    "focal_w4a16_tiles_size": (_S, [_I, _I]),
+    "focal_w4a16_tile_pack": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "focal_w4a16_tile_unpack": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "focal_w4a16_gemv_tiled": (_I, [_P, _P, _P, _I, _I, _I, _P, _S, _P]),
+    "focal_w4a16_gemv_tiled_f32": (_I, [_P, _P, _P, _I, _I, _I, _P, _S, _P]),
+    "focal_w4a16_gate_up_silu_tiled": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
     "focal_tp_buffer_size": (_S, [_I, _I, _I]),
     "focal_tp_buffer_create": (_I, [_S, ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_uint8)]),
     "focal_tp_buffer_open": (_I, [ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(_P)]),

@@ -31,8 +31,8 @@ ROOT = PKG.parent
 INCLUDE = ROOT / "include"
 BUILD = ROOT / "_build"
 LIB = PKG / "libfocal_b200.so"
-CU_SOURCES = ["capi.cu", "w4a16_gemv.cu", "gqa_decode.cu"]
-HEADERS = ["common.cuh", "host_common.h"]
+CU_SOURCES = ["capi.cu", "w4a16_gemv.cu", "w4a16_tiles.cu", "gqa_decode.cu"]
+HEADERS = ["common.cuh", "host_common.h", "w4a16_tiles.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

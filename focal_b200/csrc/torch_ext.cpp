@@ -132,6 +132,75 @@ torch::Tensor w4a16_gate_up_silu(torch::Tensor x, torch::Tensor wq_gate, torch::
   return h;
 }
 
+// Unit-tiled weights (include/focal_b200.h): tiles is a uint8 tensor of
+// focal_w4a16_tiles_size(K, N) bytes made by tile_pack.
+torch::Tensor tile_pack(torch::Tensor wq, torch::Tensor scales, torch::Tensor zeros) {
+  check_tensor(wq, "wq", at::kInt);
+  check_tensor(scales, "scales", at::kHalf);
+  check_tensor(zeros, "zeros", at::kHalf);
+  TORCH_CHECK(wq.dim() == 2, "wq must have shape [N, K / 8]");
+  const int64_t N = wq.size(0), K = wq.size(1) * 8;
+  TORCH_CHECK(scales.dim() == 2 && scales.size(0) == N && scales.size(1) == K / 128,
+              "scales must have shape [N, K / 128]");
+  TORCH_CHECK(zeros.dim() == 2 && zeros.size(0) == N && zeros.size(1) == K / 128,
+              "zeros must have shape [N, K / 128]");
+  TORCH_CHECK(K <= INT32_MAX && N <= INT32_MAX, "unsupported K/N");
+  const size_t n = focal_w4a16_tiles_size((int)K, (int)N);
+  TORCH_CHECK(n > 0, "unsupported K/N");
+  const c10::cuda::CUDAGuard guard(wq.device());
+  auto t = torch::empty({(int64_t)n}, wq.options().dtype(torch::kUInt8));
+  raise_on(focal_w4a16_tile_pack(wq.data_ptr<int32_t>(), scales.data_ptr(), zeros.data_ptr(), t.data_ptr(),
+                                 (int)K, (int)N, current_stream()));
+  return t;
+}
+
+void check_tiled(const torch::Tensor& x, const torch::Tensor& tiles, int64_t N) {
+  check_tensor(x, "x", at::kBFloat16);
+  check_tensor(tiles, "tiles", at::kByte);
+  TORCH_CHECK(x.dim() == 2, "x must have shape [M, K]");
+  TORCH_CHECK(tiles.device() == x.device(), "tiles must be on the same device as x");
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(M <= INT32_MAX && K <= INT32_MAX && N > 0 && N <= INT32_MAX, "unsupported K/N");
+  raise_on(focal_w4a16_check_shape((int)M, (int)K, (int)N));
+  TORCH_CHECK(tiles.dim() == 1 && (size_t)tiles.numel() == focal_w4a16_tiles_size((int)K, (int)N),
+              "tiles must hold focal_w4a16_tiles_size(K, N) bytes");
+}
+
+torch::Tensor w4a16_linear_tiled(torch::Tensor x, torch::Tensor tiles, int64_t N) {
+  check_tiled(x, tiles, N);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int M = (int)x.size(0), K = (int)x.size(1);
+  auto y = torch::empty({M, N}, x.options());
+  auto ws = w4a16_workspace(x, N);
+  raise_on(focal_w4a16_gemv_tiled(x.data_ptr(), tiles.data_ptr(), y.data_ptr(), M, K, (int)N, ws.data_ptr(),
+                                  ws.numel(), current_stream()));
+  return y;
+}
+
+torch::Tensor w4a16_linear_tiled_f32(torch::Tensor x, torch::Tensor tiles, int64_t N) {
+  check_tiled(x, tiles, N);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int M = (int)x.size(0), K = (int)x.size(1);
+  auto y = torch::empty({M, N}, x.options().dtype(torch::kFloat32));
+  auto ws = w4a16_workspace(x, N);
+  raise_on(focal_w4a16_gemv_tiled_f32(x.data_ptr(), tiles.data_ptr(), y.data_ptr<float>(), M, K, (int)N,
+                                      ws.data_ptr(), ws.numel(), current_stream()));
+  return y;
+}
+
+torch::Tensor w4a16_gate_up_silu_tiled(torch::Tensor x, torch::Tensor tiles_gate, torch::Tensor tiles_up,
+                                       int64_t N) {
+  check_tiled(x, tiles_gate, N);
+  check_tiled(x, tiles_up, N);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int M = (int)x.size(0), K = (int)x.size(1);
+  auto h = torch::empty({M, N}, x.options());
+  auto ws = w4a16_workspace(x, N);
+  raise_on(focal_w4a16_gate_up_silu_tiled(x.data_ptr(), tiles_gate.data_ptr(), tiles_up.data_ptr(), h.data_ptr(),
+                                          M, K, (int)N, ws.data_ptr(), ws.numel(), current_stream()));
+  return h;
+}
+
 torch::Tensor dequant(torch::Tensor wq, torch::Tensor scales, torch::Tensor zeros, int64_t K) {
   check_tensor(wq, "wq", at::kInt);
   check_tensor(scales, "scales", at::kHalf);
@@ -200,6 +269,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_linear", &w4a16_linear, "W4A16 small-M linear (B200 sm_100a)");
   m.def("w4a16_linear_f32", &w4a16_linear_f32, "W4A16 small-M linear, fp32 output");
   m.def("w4a16_gate_up_silu", &w4a16_gate_up_silu, "fused gate/up projections with SiLU(gate)*up");
+  m.def("tile_pack", &tile_pack, "re-layout W4A16 weights into the unit-tiled format");
+  m.def("w4a16_linear_tiled", &w4a16_linear_tiled, "W4A16 small-M linear on unit-tiled weights");
+  m.def("w4a16_linear_tiled_f32", &w4a16_linear_tiled_f32, "as w4a16_linear_tiled, fp32 output");
+  m.def("w4a16_gate_up_silu_tiled", &w4a16_gate_up_silu_tiled, "fused gate/up/SiLU on unit-tiled weights");
   m.def("dequant", &dequant, "fp32 dequantized weights (bit-identical to dequant_ref)");
   m.def("pack_int4", &pack_int4, "pack uint8 [N,K] nibbles into int32 [N,K/8]");
   m.def("gqa_decode_attention", &gqa_decode_attention, "contiguous GQA decode attention",

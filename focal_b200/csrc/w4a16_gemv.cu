@@ -51,6 +51,7 @@
 
 #include "common.cuh"
 #include "host_common.h"
+#include "w4a16_tiles.h"
 
 namespace focal {
 namespace gemv {
@@ -168,6 +169,8 @@ struct Params {
   int* status;
   int M, K, N, G, TS, RB, P;
   int sz_tma;   // scales / zeros by TMA quads (needs G % 8 == 0 and 16-byte aligned bases)
+  const uint8_t* tiles0;  // unit-tiled weights (w4a16_tiles.h) instead of the maps, when set
+  const uint8_t* tiles1;
   TpParams tp;  // tensor-parallel epilogues only
   long long U;  // units = RB * TS
 };
@@ -374,7 +377,7 @@ __global__ void __maxnreg__(160)
     for (int s = 0; s < kSlots; ++s) {
       // the producer's expect_tx and its activation-record arrival, plus 32
       // cp.async arrivals when scales / zeros use cp.async
-      mbar_init(full_bar + 8 * s, p.sz_tma ? 2 : 2 + 32);
+      mbar_init(full_bar + 8 * s, (p.sz_tma || p.tiles0) ? 2 : 2 + 32);
       mbar_init(empty_bar + 8 * s, 2);  // the sub-pipeline's two consumer warps
     }
     *reinterpret_cast<unsigned int*>(sm + L.flag + 16) = 0u;  // in-CTA row-block arrivals
@@ -390,7 +393,7 @@ __global__ void __maxnreg__(160)
   if (warp >= kConsumerWarps) {
     // ---------------------------------------------------------- producer
     const int pp = pair;
-    if (lane == 0) {
+    if (lane == 0 && !p.tiles0) {
       prefetch_tensormap(&tmap0);
       if (NW == 2) prefetch_tensormap(&tmap1);
       if (p.sz_tma) {
@@ -410,6 +413,19 @@ __global__ void __maxnreg__(160)
     auto issue_unit = [&](int j, int rb, int st, bool opens_quad, int qs) {
       const int slot = pp * R + j % R;
       const uint32_t fb = full_bar + 8 * slot;
+      if (p.tiles0) {
+        // unit-tiled: the weight image and the unit's scales / zeros are one
+        // contiguous chunk per matrix, fetched with two 1-D bulk copies
+        mbar_arrive_expect_tx(fb, NW * tiles::kTileBytes);
+#pragma unroll
+        for (int mat = 0; mat < NW; ++mat) {
+          const uint8_t* src = (mat == 0 ? p.tiles0 : p.tiles1) + ((size_t)rb * p.TS + st) * tiles::kTileBytes;
+          bulk_load(base + L.w + (slot * NW + mat) * kRows * 128, src, tiles::kWeightBytes, fb);
+          bulk_load(base + L.sz + (slot * NW + mat) * tiles::kGroupBytes, src + tiles::kScalesOffset,
+                    tiles::kGroupBytes, fb);
+        }
+        return;
+      }
       const bool szq = p.sz_tma && opens_quad;
       mbar_arrive_expect_tx(fb, NW * kRows * 128 + (szq ? NW * 2 * kRows * 16 : 0));
       tma_load_2d(base + L.w + (slot * NW + 0) * kRows * 128, &tmap0, st * kWordsPerStage, rb * kRows, fb, pol);
@@ -501,7 +517,7 @@ __global__ void __maxnreg__(160)
           if (lane == 0) mbar_arrive(fb);  // the record's arrival (release: orders the writes above)
 #pragma unroll
           for (int m = 0; m < MTp; ++m) xcur[m] = xnext[m];
-          if (!p.sz_tma) {
+          if (!p.sz_tma && !p.tiles0) {
             // scale / zero pairs (groups 2st, 2st+1) of the 64 rows: 4 bytes each
             const int row0 = rb * kRows;
 #pragma unroll
@@ -1021,9 +1037,13 @@ int tp_params(const focal_tp_comm* comm, int M, int N, TpParams* tp) {
   return FOCAL_OK;
 }
 
+// One call.  The weights are either the reference layout (wq, scales, zeros
+// per matrix; TMA tensor maps) or, when t0 is set, unit-tiled (t0 / t1; bulk
+// copies).
 int run(int epi, const void* x, const int32_t* wq0, const void* s0, const void* z0,
         const int32_t* wq1, const void* s1, const void* z1, void* y, int M, int K, int N,
-        void* workspace, size_t ws_bytes, cudaStream_t stream, const focal_tp_comm* comm = nullptr) {
+        void* workspace, size_t ws_bytes, cudaStream_t stream, const focal_tp_comm* comm = nullptr,
+        const void* t0 = nullptr, const void* t1 = nullptr) {
   clear_error();
   int rc = check_shape(M, K, N);
   if (rc) return rc;
@@ -1033,13 +1053,20 @@ int run(int epi, const void* x, const int32_t* wq0, const void* s0, const void* 
     if (rc) return rc;
   }
   const int NW = epi == kEpiSiluMul ? 2 : 1;
-  if (!x || !wq0 || !s0 || !z0 || !y || (NW == 2 && (!wq1 || !s1 || !z1)))
-    return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
+  const bool tiled = t0 != nullptr;
+  if (tiled) {
+    if (!x || !y || (NW == 2 && !t1)) return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
+    if (!aligned(t0, 16) || (NW == 2 && !aligned(t1, 16)))
+      return set_error(FOCAL_ERR_INVALID_VALUE, "tiles must be 16-byte aligned");
+  } else {
+    if (!x || !wq0 || !s0 || !z0 || !y || (NW == 2 && (!wq1 || !s1 || !z1)))
+      return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
+    if (!aligned(wq0, 16) || (NW == 2 && !aligned(wq1, 16)))
+      return set_error(FOCAL_ERR_INVALID_VALUE, "wq must be 16-byte aligned");
+    if (!aligned(s0, 4) || !aligned(z0, 4) || (NW == 2 && (!aligned(s1, 4) || !aligned(z1, 4))))
+      return set_error(FOCAL_ERR_INVALID_VALUE, "scales and zeros must be 4-byte aligned");
+  }
   if (!aligned(x, 16)) return set_error(FOCAL_ERR_INVALID_VALUE, "x must be 16-byte aligned");
-  if (!aligned(wq0, 16) || (NW == 2 && !aligned(wq1, 16)))
-    return set_error(FOCAL_ERR_INVALID_VALUE, "wq must be 16-byte aligned");
-  if (!aligned(s0, 4) || !aligned(z0, 4) || (NW == 2 && (!aligned(s1, 4) || !aligned(z1, 4))))
-    return set_error(FOCAL_ERR_INVALID_VALUE, "scales and zeros must be 4-byte aligned");
   if (!aligned(y, epi == kEpiF32 ? 4 : 2)) return set_error(FOCAL_ERR_INVALID_VALUE, "y is misaligned");
   if (!workspace) return set_error(FOCAL_ERR_WORKSPACE, "workspace missing");
   if (!aligned(workspace, 256)) return set_error(FOCAL_ERR_INVALID_VALUE, "workspace must be 256-byte aligned");
@@ -1049,25 +1076,29 @@ int run(int epi, const void* x, const int32_t* wq0, const void* s0, const void* 
   if (rc) return rc;
   const int MT = mt_for(M);
 
-  // maps: weights 0 / 1, then scales 0, zeros 0, scales 1, zeros 1
-  CUtensorMap maps[6];
-  const int32_t* wqs[2] = {wq0, NW == 2 ? wq1 : wq0};
-  const void* szs[4] = {s0, z0, NW == 2 ? s1 : s0, NW == 2 ? z1 : z0};
-  for (int m = 0; m < 2; ++m) {
-    rc = tensor_map(kTmapWeights, wqs[m], K, N, dev.device, &maps[m]);
-    if (rc) return rc;
-  }
-  // Scales and zeros come in by TMA when each row's groups form 16-byte
-  // multiples (K % 1024 == 0) and the bases are 16-byte aligned; otherwise
-  // by 4-byte cp.async.
-  bool sz_tma = (K / 128) % kSzQuadGroups == 0;
-  for (int j = 0; j < 4; ++j) sz_tma = sz_tma && aligned(szs[j], 16);
-  for (int j = 0; j < 4; ++j) {
-    if (sz_tma) {
-      rc = tensor_map(kTmapGroups, szs[j], K, N, dev.device, &maps[2 + j]);
+  // maps: weights 0 / 1, then scales 0, zeros 0, scales 1, zeros 1 (unused,
+  // left zero, for tiled weights)
+  CUtensorMap maps[6] = {};
+  bool sz_tma = false;
+  if (!tiled) {
+    const int32_t* wqs[2] = {wq0, NW == 2 ? wq1 : wq0};
+    const void* szs[4] = {s0, z0, NW == 2 ? s1 : s0, NW == 2 ? z1 : z0};
+    for (int m = 0; m < 2; ++m) {
+      rc = tensor_map(kTmapWeights, wqs[m], K, N, dev.device, &maps[m]);
       if (rc) return rc;
-    } else {
-      maps[2 + j] = maps[0];  // unused
+    }
+    // Scales and zeros come in by TMA when each row's groups form 16-byte
+    // multiples (K % 1024 == 0) and the bases are 16-byte aligned; otherwise
+    // by 4-byte cp.async.
+    sz_tma = (K / 128) % kSzQuadGroups == 0;
+    for (int j = 0; j < 4; ++j) sz_tma = sz_tma && aligned(szs[j], 16);
+    for (int j = 0; j < 4; ++j) {
+      if (sz_tma) {
+        rc = tensor_map(kTmapGroups, szs[j], K, N, dev.device, &maps[2 + j]);
+        if (rc) return rc;
+      } else {
+        maps[2 + j] = maps[0];  // unused
+      }
     }
   }
   Params p{};
@@ -1085,6 +1116,8 @@ int run(int epi, const void* x, const int32_t* wq0, const void* s0, const void* 
   p.RB = N / kRows;
   p.U = (long long)p.TS * p.RB;
   p.sz_tma = sz_tma ? 1 : 0;
+  p.tiles0 = static_cast<const uint8_t*>(t0);
+  p.tiles1 = static_cast<const uint8_t*>(NW == 2 ? t1 : t0);
   p.tp = tp;
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* ws = static_cast<uint8_t*>(workspace);
@@ -1207,6 +1240,24 @@ int focal_w4a16_gemv_allreduce(const void* x, const int32_t* wq, const void* sca
                                size_t ws_bytes, cudaStream_t stream) {
   return gemv::run(gemv::kEpiAllReduce, x, wq, scales, zeros, nullptr, nullptr, nullptr, y, M, K, N,
                    workspace, ws_bytes, stream, comm);
+}
+
+int focal_w4a16_gemv_tiled(const void* x, const void* tiles, void* y, int M, int K, int N, void* workspace,
+                           size_t ws_bytes, cudaStream_t stream) {
+  return gemv::run(gemv::kEpiBf16, x, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, y, M, K, N, workspace,
+                   ws_bytes, stream, nullptr, tiles);
+}
+
+int focal_w4a16_gemv_tiled_f32(const void* x, const void* tiles, float* y, int M, int K, int N, void* workspace,
+                               size_t ws_bytes, cudaStream_t stream) {
+  return gemv::run(gemv::kEpiF32, x, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, y, M, K, N, workspace,
+                   ws_bytes, stream, nullptr, tiles);
+}
+
+int focal_w4a16_gate_up_silu_tiled(const void* x, const void* tiles_gate, const void* tiles_up, void* h, int M,
+                                   int K, int N, void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  return gemv::run(gemv::kEpiSiluMul, x, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, h, M, K, N,
+                   workspace, ws_bytes, stream, nullptr, tiles_gate, tiles_up);
 }
 
 int focal_w4a16_gemv_noalloc(const void* x, const int32_t* wq, const void* scales, const void* zeros,

@@ -108,6 +108,35 @@ int focal_w4a16_gate_up_silu(const void* x, const int32_t* wq_gate, const void* 
                              const void* zeros_up, void* h, int M, int K, int N, void* workspace,
                              size_t ws_bytes, cudaStream_t stream);
 
+/* ------------------------------------------------- unit-tiled weights ---
+ * An offline re-layout of (wq, scales, zeros) for the linears below (the
+ * reference lists a tensor-core-friendly re-layout as next work and has no
+ * counterpart).  Unit u = rb * (K/256) + st (64 weight rows x 256 K values)
+ * is one contiguous 8704-byte chunk: its 64 x 32 packed words in the order a
+ * 128-byte-swizzled copy leaves them in shared memory (row r at byte 128 r,
+ * 16-byte chunk c at position c ^ (r & 7)), then the rows' two scales
+ * (4 bytes a row), then their two zeros.  Each unit of the GEMV is then one
+ * contiguous read.  Contract: N % 64 == 0, K % 256 == 0; tiles 16-byte
+ * aligned, wq 16-byte, scales and zeros 4-byte aligned.
+ */
+size_t focal_w4a16_tiles_size(int K, int N);   /* bytes; 0 outside the contract */
+int focal_w4a16_tile_pack(const int32_t* wq, const void* scales, const void* zeros, void* tiles, int K, int N,
+                          cudaStream_t stream);
+/* The inverse: recovers the reference packing bit for bit. */
+int focal_w4a16_tile_unpack(const void* tiles, int32_t* wq, void* scales, void* zeros, int K, int N,
+                            cudaStream_t stream);
+
+/* The linear layer, its fp32-output form and the fused gate/up/SiLU on
+ * unit-tiled weights: the same results, bit for bit, as focal_w4a16_gemv,
+ * focal_w4a16_gemv_f32 and focal_w4a16_gate_up_silu on the weights the tiles
+ * were packed from.  Same shape contract and workspace rules. */
+int focal_w4a16_gemv_tiled(const void* x, const void* tiles, void* y, int M, int K, int N, void* workspace,
+                           size_t ws_bytes, cudaStream_t stream);
+int focal_w4a16_gemv_tiled_f32(const void* x, const void* tiles, float* y, int M, int K, int N, void* workspace,
+                               size_t ws_bytes, cudaStream_t stream);
+int focal_w4a16_gate_up_silu_tiled(const void* x, const void* tiles_gate, const void* tiles_up, void* h, int M,
+                                   int K, int N, void* workspace, size_t ws_bytes, cudaStream_t stream);
+
 /* ---------------------------------------- tensor-parallel fused linears ---
  * New entry points (the reference has no multi-GPU code): the linear layer
  * with its collective in the same kernel.  Each 64-row block, once finished,

@@ -127,6 +127,52 @@ def linear_f64(x_bf16: np.ndarray, wq: np.ndarray, scales: np.ndarray,
     return x @ w.T
 
 
+# -------------------------------------------------------- unit-tiled format
+# Not a reference format: the re-layout the reference lists as next work
+# (docs/blog_notes.md:193-213), restated here so the device packer can be
+# checked byte for byte; its inverse must give back the reference packing.
+TILE_BYTES = 8704
+
+
+def tile_pack(wq: np.ndarray, scales: np.ndarray, zeros: np.ndarray, K: int) -> np.ndarray:
+    """(wq [N, K/8] int32, scales / zeros [N, K/128] fp16) -> uint8 tiles.
+
+    Unit u = rb * (K/256) + st, 8704 bytes: 64 rows x 32 words with row r at
+    byte 128 r and its 16-byte chunk c at position c ^ (r & 7); then the rows'
+    scale pairs (groups 2 st, 2 st + 1, 4 bytes a row), then their zero pairs.
+    """
+    N = wq.shape[0]
+    RB, TS = N // 64, K // 256
+    w = np.ascontiguousarray(wq).view(np.uint32).reshape(RB, 64, TS, 8, 4)   # [rb, r, st, c, word]
+    w = w.transpose(0, 2, 1, 3, 4)                                          # [rb, st, r, c, word]
+    r = np.arange(64)[:, None]
+    pos = np.arange(8)[None, :]
+    c_at_pos = pos ^ (r & 7)                                                # chunk stored at position
+    w = np.take_along_axis(w, np.broadcast_to(c_at_pos[None, None, :, :, None], w.shape), axis=3)
+    sz = [np.ascontiguousarray(a).view(np.uint32).reshape(RB, 64, TS).transpose(0, 2, 1)
+          for a in (scales, zeros)]                                         # [rb, st, r]
+    out = np.empty((RB, TS, TILE_BYTES // 4), dtype=np.uint32)
+    out[:, :, :2048] = w.reshape(RB, TS, 2048)
+    out[:, :, 2048:2112] = sz[0]
+    out[:, :, 2112:2176] = sz[1]
+    return out.reshape(-1).view(np.uint8)
+
+
+def tile_unpack(tiles: np.ndarray, K: int, N: int):
+    """Inverse of tile_pack: (wq int32 [N, K/8], scales fp16, zeros fp16)."""
+    RB, TS = N // 64, K // 256
+    t = np.ascontiguousarray(tiles).view(np.uint32).reshape(RB, TS, TILE_BYTES // 4)
+    w = t[:, :, :2048].reshape(RB, TS, 64, 8, 4)
+    r = np.arange(64)[:, None]
+    c = np.arange(8)[None, :]
+    pos_of_c = c ^ (r & 7)                                                  # position holding chunk c
+    w = np.take_along_axis(w, np.broadcast_to(pos_of_c[None, None, :, :, None], w.shape), axis=3)
+    wq = w.transpose(0, 2, 1, 3, 4).reshape(N, K // 8).view(np.int32)
+    sc = t[:, :, 2048:2112].transpose(0, 2, 1).reshape(N, K // 256).copy().view(np.float16)
+    ze = t[:, :, 2112:2176].transpose(0, 2, 1).reshape(N, K // 256).copy().view(np.float16)
+    return np.ascontiguousarray(wq), sc, ze
+
+
 # ---------------------------------------------------------------- generators
 def baseline_case(M: int, K: int, N: int, seed: int):
     """Inputs with the benchmark's value distributions, drawn by numpy.

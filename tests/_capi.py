@@ -85,3 +85,36 @@ def attention(q, k, v, scale=None, ws=None):
     _lib.call("focal_gqa_decode_attn", ptr(q), ptr(k), ptr(v), ptr(o), B, Hq, Hkv, L, D,
               float(scale), ptr(buf), n, stream_ptr())
     return o
+
+
+def tile_pack(wq, scales, zeros):
+    N, K = wq.shape[0], wq.shape[1] * 8
+    t = torch.empty(int(_lib.lib().focal_w4a16_tiles_size(K, N)), dtype=torch.uint8, device=wq.device)
+    _lib.call("focal_w4a16_tile_pack", ptr(wq), ptr(scales), ptr(zeros), ptr(t), K, N, stream_ptr())
+    return t
+
+
+def tile_unpack(t, K, N):
+    wq = torch.empty((N, K // 8), dtype=torch.int32, device=t.device)
+    s = torch.empty((N, K // 128), dtype=torch.float16, device=t.device)
+    z = torch.empty((N, K // 128), dtype=torch.float16, device=t.device)
+    _lib.call("focal_w4a16_tile_unpack", ptr(t), ptr(wq), ptr(s), ptr(z), K, N, stream_ptr())
+    return wq, s, z
+
+
+def gemv_tiled(x, tiles, N, out_dtype=torch.bfloat16):
+    M, K = x.shape
+    y = torch.empty((M, N), dtype=out_dtype, device=x.device)
+    buf, n = w4a16_workspace(M, K, N, x.device)
+    name = "focal_w4a16_gemv_tiled" if out_dtype == torch.bfloat16 else "focal_w4a16_gemv_tiled_f32"
+    _lib.call(name, ptr(x), ptr(tiles), ptr(y), M, K, N, ptr(buf), n, stream_ptr())
+    return y
+
+
+def gate_up_silu_tiled(x, tiles_gate, tiles_up, N):
+    M, K = x.shape
+    h = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    buf, n = w4a16_workspace(M, K, N, x.device)
+    _lib.call("focal_w4a16_gate_up_silu_tiled", ptr(x), ptr(tiles_gate), ptr(tiles_up), ptr(h), M, K, N,
+              ptr(buf), n, stream_ptr())
+    return h
