@@ -199,6 +199,20 @@ def gqa_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.
     return _ext().gqa_decode_attention(q, k_cache, v_cache, scale)
 
 
+def gqa_decode_attention_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
+                               block_table: torch.Tensor, seq_lens: torch.Tensor, max_seq_len: int,
+                               scale: float | None = None) -> torch.Tensor:
+    """Decode attention over a paged KV cache with per-sequence lengths.
+
+    k_pages / v_pages [num_pages, Hkv, page_size, D] bf16 (page_size 16, 32 or
+    a multiple of 64); block_table int32 [B, max_pages] maps page j of
+    sequence b to a page; seq_lens int32 [B] in 1..max_seq_len.  max_seq_len
+    (a host integer, an upper bound on seq_lens) sizes the launch.  Returns
+    o [B, Hq, D] bf16.
+    """
+    return _ext().gqa_decode_attention_paged(q, k_pages, v_pages, block_table, seq_lens, max_seq_len, scale)
+
+
 __all__ = [
     "SUPPORTED_K",
     "SUPPORTED_M",
@@ -209,6 +223,7 @@ __all__ = [
     "decode_mlp",
     "dequant_ref",
     "gqa_decode_attention",
+    "gqa_decode_attention_paged",
     "pack_int4_weight",
     "random_case",
     "require_cuda_contiguous",

@@ -60,6 +60,7 @@ SIGNATURES = {
     "focal_pack_int4": (_I, [_P, _P, _I, _I, _P]),
     "focal_gqa_decode_workspace_size": (_S, [_I, _I, _I, _I, _I]),
     "focal_gqa_decode_attn": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _S, _P]),
+    "focal_gqa_decode_paged": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S, _P]),
     "focal_device_status": (_I, [ctypes.POINTER(_I)]),
     "focal_reset_device_status": (_I, []),
 }

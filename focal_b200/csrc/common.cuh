@@ -18,6 +18,7 @@ enum DeviceStatus : int {
   kDevOk = 0,
   kDevWaitTimeout = 1,  // a bounded mbarrier wait gave up
   kDevPeerTimeout = 2,  // a tensor-parallel peer did not signal in time
+  kDevBadIndex = 3,     // a paged-KV block-table entry or sequence length was out of range
 };
 
 // ~2^31 SM cycles (about one second at 1.9 GHz) before a wait gives up.
@@ -110,6 +111,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
       "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// 4-D tiled TMA load into this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(policy)
       : "memory");
 }
 

@@ -17,6 +17,19 @@
 //  * online softmax in the log2 domain per warp, merged across the four warps
 //    in shared memory, then across splits by the last CTA to finish (an
 //    arrival counter per (b, kv head) in the caller's workspace).
+//
+// Paged variant (PAGED = true): the caches are pages [num_pages, Hkv,
+// page_size, 128] shared by all sequences, a block table maps page j of
+// sequence b to its page, and each sequence has its own length.  The
+// producer warp looks the pages up (32 block-table entries per warp-wide
+// load) and loads each tile with 4-D TMA boxes of min(page_size, 64) rows,
+// so shared memory holds the same swizzled tile as in the contiguous case
+// (16-row pages need 16 boxes per tile and run about 21% below contiguous
+// speed; 64-row and larger pages match it).  Rows past a sequence's end are
+// masked in S; their V rows are zeroed in shared memory before P V (a stale
+// NaN times p = 0 would still be NaN).  A sequence uses only the splits its
+// length needs; block-table entries or lengths out of range set the device
+// status (kDevBadIndex) and are clamped.
 #include <cmath>
 
 #include "common.cuh"
@@ -37,13 +50,16 @@ constexpr int kMaxSplits = 128;
 constexpr int kCounterBytes = 256;     // counters region granularity
 
 struct Params {
+  const int32_t* block_table;  // paged: [B, max_pages]
+  const int32_t* seq_lens;     // paged: [B], 1 .. L
+  int page_size, max_pages, num_pages;
   const __nv_bfloat16* q;
   __nv_bfloat16* o;
   float* part_o;   // [BH][S][grp][128]
   float* part_ml;  // [BH][S][grp][2]  (max in log2 domain, sum)
   unsigned int* counters;  // [BH]
   int* status;
-  int Hq, Hkv, grp, L, tiles, tiles_per_split, splits;
+  int Hq, Hkv, grp, L, tiles, tiles_per_split, splits;  // paged: L is the longest allowed sequence
   float scale_log2;
 };
 
@@ -66,6 +82,7 @@ __device__ __forceinline__ uint32_t tile_off(int p, int c) {
   return (c >> 3) * kHalfBytes + p * 128 + (((c & 7) ^ (p & 7)) << 4);
 }
 
+template <bool PAGED>
 __global__ void __launch_bounds__(kThreads, 2)
     gqa_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v, const Params p) {
@@ -85,7 +102,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int b = bh / p.Hkv;
   const int kvh = bh - b * p.Hkv;
   const int t0 = split * p.tiles_per_split;
-  const int nt = min(p.tiles, t0 + p.tiles_per_split) - t0;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -107,7 +123,76 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   griddep_wait();
 
-  if (warp == kConsumerWarps) {
+  // this sequence's length, tiles and splits (all of the grid's for contiguous caches)
+  int L = p.L;
+  if (PAGED) {
+    L = p.seq_lens[b];
+    if (L < 1 || L > p.L) {
+      if (threadIdx.x == 0 && split == 0) atomicExch(p.status, kDevBadIndex);
+      L = L < 1 ? 1 : p.L;
+    }
+  }
+  const int tiles = PAGED ? (L + kTile - 1) / kTile : p.tiles;
+  const int splits = PAGED ? (tiles + p.tiles_per_split - 1) / p.tiles_per_split : p.splits;
+  const int nt = min(tiles, t0 + p.tiles_per_split) - t0;
+  if (nt <= 0) return;  // a split past this sequence's end: nothing to do, no arrival
+
+  if (PAGED && warp == kConsumerWarps) {
+    // ------------------------------------------------------ paged producer
+    const int rows = p.page_size >= kTile ? kTile : p.page_size;  // rows per box
+    const int32_t* bt = p.block_table + (size_t)b * p.max_pages;
+    const int first_page = (t0 * kTile) / p.page_size;
+    const int last_page = (L - 1) / p.page_size;
+    int chunk = -1, my_id = 0;
+    // page id of page `pj` of the sequence (warp-uniform pj >= first_page),
+    // from 32 block-table entries loaded by the warp at a time
+    auto page_id = [&](int pj) {
+      const int c = (pj - first_page) >> 5;
+      if (c != chunk) {
+        chunk = c;
+        const int q = first_page + 32 * c + lane;
+        my_id = q <= last_page ? bt[q] : 0;
+        if (my_id < 0 || my_id >= p.num_pages) {
+          atomicExch(p.status, kDevBadIndex);
+          my_id = 0;
+        }
+      }
+      return __shfl_sync(0xffffffffu, my_id, (pj - first_page) & 31);
+    };
+    const uint64_t pol = l2_policy_evict_first();
+    bool ok = true;
+    for (int i = 0; i < nt; ++i) {
+      const int slot = i % kStages;
+      if (i >= kStages) {
+        bool w = true;
+        if (lane == 0) w = mbar_wait_bounded(empty_bar + 8 * slot, ((i / kStages) - 1) & 1);
+        if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
+          ok = false;
+          break;
+        }
+      }
+      const uint32_t fb = full_bar + 8 * slot;
+      const uint32_t dst = ring + slot * kKVStageBytes;
+      const int pos = (t0 + i) * kTile;
+      // pages of this tile that hold positions < L (boxes past the end are not loaded)
+      const int npg = rows == kTile ? 1 : min(kTile / rows, (L - pos + rows - 1) / rows);
+      const int row0 = rows == kTile ? pos % p.page_size : 0;
+      if (lane == 0) mbar_arrive_expect_tx(fb, npg * 4 * rows * 128);
+      for (int j = 0; j < npg; ++j) {
+        const int id = page_id(pos / p.page_size + j);
+        if (lane == 0) {
+          const uint32_t dj = dst + j * rows * 128;
+          tma_load_4d(dj + 0 * kHalfBytes, &tmap_k, 0, row0, kvh, id, fb, pol);
+          tma_load_4d(dj + 1 * kHalfBytes, &tmap_k, 64, row0, kvh, id, fb, pol);
+          tma_load_4d(dj + 2 * kHalfBytes, &tmap_v, 0, row0, kvh, id, fb, pol);
+          tma_load_4d(dj + 3 * kHalfBytes, &tmap_v, 64, row0, kvh, id, fb, pol);
+        }
+      }
+    }
+    if (!ok && lane == 0 && p.status) atomicExch(p.status, kDevWaitTimeout);
+    return;
+  }
+  if (!PAGED && warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
     bool ok = true;
     if (lane == 0) {
@@ -167,6 +252,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     const uint32_t kt = ring + slot * kKVStageBytes;
     const uint32_t vt = kt + 2 * kHalfBytes;
+    if (PAGED && (t0 + i) * kTile + pw + 15 >= L) {
+      // zero this warp's V rows past the sequence's end (loaded from the rest
+      // of a page, or left from an earlier tile when their page was skipped)
+      const int p0 = (t0 + i) * kTile + pw;
+      for (int e = lane; e < 16 * 16; e += 32) {
+        const int r = e >> 4, c = e & 15;
+        if (p0 + r >= L) sts128(vt + tile_off(pw + r, c), make_uint4(0u, 0u, 0u, 0u));
+      }
+      __syncwarp();
+    }
 
     // ---- S = Q K^T for positions pw .. pw+15 (two n-tiles of 8)
     float sacc[2][4];
@@ -190,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int pos = pos0 + 8 * n2 + 2 * t + (j & 1);
-        const float s = pos < p.L ? sacc[n2][j] * p.scale_log2 : -INFINITY;
+        const float s = pos < L ? sacc[n2][j] * p.scale_log2 : -INFINITY;
         sacc[n2][j] = s;
         mt[j >> 1] = fmaxf(mt[j >> 1], s);
       }
@@ -285,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       acc.w += wgt * v.w;
       l += wgt * warp_ml[(w * kMaxGroup + row) * 2 + 1];
     }
-    if (p.splits == 1) {
+    if (splits == 1) {
       const float inv = 1.0f / l;
       __nv_bfloat16* dst = p.o + ((size_t)b * p.Hq + (size_t)kvh * grp + row) * kD + d;
       *reinterpret_cast<uint2*>(dst) =
@@ -296,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (d == 0) *reinterpret_cast<float2*>(p.part_ml + rec * 2) = make_float2(mm, l);
     }
   }
-  if (p.splits == 1) return;
+  if (splits == 1) return;
 
   // ---- split combine by the last CTA of this (b, kv head)
   named_barrier(1, kConsumerWarps * 32);
@@ -305,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // CTA the same increment and the barrier after it order its loads.
   if (ctid == 0) {
     const unsigned int prev = atom_add_acq_rel_gpu(p.counters + bh, 1u);
-    *last_flag = (prev == (unsigned int)(p.splits - 1));
+    *last_flag = (prev == (unsigned int)(splits - 1));
   }
   named_barrier(1, kConsumerWarps * 32);
   if (!*last_flag) return;
@@ -314,11 +409,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int d = (e - row * (kD / 4)) * 4;
     const size_t rec0 = (size_t)bh * p.splits * grp + row;
     float mm = -INFINITY;
-    for (int s = 0; s < p.splits; ++s) mm = fmaxf(mm, __ldcg(p.part_ml + (rec0 + (size_t)s * grp) * 2));
+    for (int s = 0; s < splits; ++s) mm = fmaxf(mm, __ldcg(p.part_ml + (rec0 + (size_t)s * grp) * 2));
     const float mu = mm == -INFINITY ? 0.f : mm;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float l = 0.f;
-    for (int s = 0; s < p.splits; ++s) {
+    for (int s = 0; s < splits; ++s) {
       const size_t rec = rec0 + (size_t)s * grp;
       const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + rec * 2));
       const float wgt = fast_exp2(ml.x - mu);
@@ -377,6 +472,57 @@ int check(int B, int Hq, int Hkv, int L, int D) {
   return FOCAL_OK;
 }
 
+// Parameters common to both layouts; the split partials and counters come
+// from the workspace when the plan splits the sequence.
+int fill_params(Params* pp, const void* q, void* o, int B, int Hq, int Hkv, int L, float scale, const Plan& pl,
+                void* workspace, size_t ws_bytes, const DeviceInfo& dev) {
+  Params& p = *pp;
+  p = Params{};
+  const int grp = Hq / Hkv;
+  const int bhn = B * Hkv;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.o = static_cast<__nv_bfloat16*>(o);
+  if (pl.splits > 1) {
+    const size_t need = workspace_size(B, Hq, Hkv, L);
+    if (!workspace || ws_bytes < need)
+      return set_error(FOCAL_ERR_WORKSPACE, "workspace too small: need %zu bytes, got %zu", need, ws_bytes);
+    if (!aligned(workspace, 256)) return set_error(FOCAL_ERR_INVALID_VALUE, "workspace must be 256-byte aligned");
+    const size_t counters = ((size_t)bhn * 4 + kCounterBytes - 1) / kCounterBytes * kCounterBytes;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    p.counters = reinterpret_cast<unsigned int*>(ws);
+    p.part_o = reinterpret_cast<float*>(ws + counters);
+    p.part_ml = p.part_o + (size_t)bhn * pl.splits * grp * kD;
+  }
+  p.status = dev.status;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.grp = grp;
+  p.L = L;
+  p.tiles = pl.tiles;
+  p.tiles_per_split = pl.tiles_per_split;
+  p.splits = pl.splits;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  return FOCAL_OK;
+}
+
+template <bool PAGED>
+int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, int bhn, cudaStream_t stream) {
+  auto kern = gqa_decode_kernel<PAGED>;
+  int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), PAGED ? 41 : 40, kSmemBytes);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits, bhn, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, mk, mv, p), "gqa_decode_kernel launch");
+}
+
 }  // namespace attn
 }  // namespace focal
 
@@ -404,35 +550,10 @@ int focal_gqa_decode_attn(const void* q, const void* k, const void* v, void* o, 
   rc = current_device_info(&dev);
   if (rc) return rc;
   const attn::Plan pl = attn::make_plan(B, Hkv, L, dev.sm_count);
-  const int grp = Hq / Hkv;
   const int bhn = B * Hkv;
-
   attn::Params p;
-  p.q = static_cast<const __nv_bfloat16*>(q);
-  p.o = static_cast<__nv_bfloat16*>(o);
-  p.part_o = nullptr;
-  p.part_ml = nullptr;
-  p.counters = nullptr;
-  if (pl.splits > 1) {
-    const size_t need = attn::workspace_size(B, Hq, Hkv, L);
-    if (!workspace || ws_bytes < need)
-      return set_error(FOCAL_ERR_WORKSPACE, "workspace too small: need %zu bytes, got %zu", need, ws_bytes);
-    if (!aligned(workspace, 256)) return set_error(FOCAL_ERR_INVALID_VALUE, "workspace must be 256-byte aligned");
-    const size_t counters = ((size_t)bhn * 4 + attn::kCounterBytes - 1) / attn::kCounterBytes * attn::kCounterBytes;
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    p.counters = reinterpret_cast<unsigned int*>(ws);
-    p.part_o = reinterpret_cast<float*>(ws + counters);
-    p.part_ml = p.part_o + (size_t)bhn * pl.splits * grp * attn::kD;
-  }
-  p.status = dev.status;
-  p.Hq = Hq;
-  p.Hkv = Hkv;
-  p.grp = grp;
-  p.L = L;
-  p.tiles = pl.tiles;
-  p.tiles_per_split = pl.tiles_per_split;
-  p.splits = pl.splits;
-  p.scale_log2 = scale * 1.4426950408889634f;
+  rc = attn::fill_params(&p, q, o, B, Hq, Hkv, L, scale, pl, workspace, ws_bytes, dev);
+  if (rc) return rc;
 
   CUtensorMap mk, mv;
   const uint64_t dims[3] = {(uint64_t)attn::kD, (uint64_t)L, (uint64_t)bhn};
@@ -445,19 +566,56 @@ int focal_gqa_decode_attn(const void* q, const void* k, const void* v, void* o, 
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
 
-  rc = ensure_dynamic_smem(reinterpret_cast<const void*>(attn::gqa_decode_kernel), 40, attn::kSmemBytes);
+  return attn::launch<false>(mk, mv, p, bhn, stream);
+}
+
+int focal_gqa_decode_paged(const void* q, const void* k_pages, const void* v_pages, const int32_t* block_table,
+                           const int32_t* seq_lens, void* o, int B, int Hq, int Hkv, int D, int num_pages,
+                           int page_size, int max_pages_per_seq, int max_seq_len, float scale, void* workspace,
+                           size_t ws_bytes, cudaStream_t stream) {
+  clear_error();
+  int rc = attn::check(B, Hq, Hkv, max_seq_len, D);
   if (rc) return rc;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.splits, bhn, 1);
-  cfg.blockDim = dim3(attn::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = attn::kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, attn::gqa_decode_kernel, mk, mv, p), "gqa_decode_kernel launch");
+  if (page_size < 16 || page_size % 16 != 0 || (attn::kTile % page_size != 0 && page_size % attn::kTile != 0))
+    return set_error(FOCAL_ERR_UNSUPPORTED, "page_size must be 16, 32 or a multiple of 64");
+  if (num_pages < 1 || max_pages_per_seq < 1)
+    return set_error(FOCAL_ERR_UNSUPPORTED, "num_pages and max_pages_per_seq must be positive");
+  if ((long long)max_pages_per_seq * page_size < max_seq_len)
+    return set_error(FOCAL_ERR_UNSUPPORTED, "max_seq_len exceeds max_pages_per_seq * page_size");
+  if (!q || !k_pages || !v_pages || !block_table || !seq_lens || !o)
+    return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
+  if (!aligned(q, 4) || !aligned(o, 8) || !aligned(k_pages, 16) || !aligned(v_pages, 16) ||
+      !aligned(block_table, 4) || !aligned(seq_lens, 4))
+    return set_error(FOCAL_ERR_INVALID_VALUE, "q/o must be 8-byte, pages 16-byte, tables 4-byte aligned");
+  if (!(scale > 0.f) || !std::isfinite(scale))
+    return set_error(FOCAL_ERR_INVALID_VALUE, "scale must be positive and finite");
+  DeviceInfo dev;
+  rc = current_device_info(&dev);
+  if (rc) return rc;
+  const attn::Plan pl = attn::make_plan(B, Hkv, max_seq_len, dev.sm_count);
+  const int bhn = B * Hkv;
+  attn::Params p;
+  rc = attn::fill_params(&p, q, o, B, Hq, Hkv, max_seq_len, scale, pl, workspace, ws_bytes, dev);
+  if (rc) return rc;
+  p.block_table = block_table;
+  p.seq_lens = seq_lens;
+  p.page_size = page_size;
+  p.max_pages = max_pages_per_seq;
+  p.num_pages = num_pages;
+
+  // [num_pages, Hkv, page_size, 128] pages; boxes of 64 dims x min(page_size, 64) rows
+  CUtensorMap mk, mv;
+  const uint64_t dims[4] = {(uint64_t)attn::kD, (uint64_t)page_size, (uint64_t)Hkv, (uint64_t)num_pages};
+  const uint64_t strides[3] = {(uint64_t)attn::kD * 2, (uint64_t)page_size * attn::kD * 2,
+                               (uint64_t)Hkv * page_size * attn::kD * 2};
+  const uint32_t box[4] = {64, (uint32_t)(page_size < attn::kTile ? page_size : attn::kTile), 1, 1};
+  rc = encode_tensor_map(&mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, k_pages, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tensor_map(&mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v_pages, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  return attn::launch<true>(mk, mv, p, bhn, stream);
 }
 
 }  // extern "C"

@@ -263,6 +263,43 @@ torch::Tensor gqa_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch
   return o;
 }
 
+torch::Tensor gqa_decode_attention_paged(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pages,
+                                         torch::Tensor block_table, torch::Tensor seq_lens, int64_t max_seq_len,
+                                         c10::optional<double> scale) {
+  check_tensor(q, "q", at::kBFloat16);
+  check_tensor(k_pages, "k_pages", at::kBFloat16);
+  check_tensor(v_pages, "v_pages", at::kBFloat16);
+  check_tensor(block_table, "block_table", at::kInt);
+  check_tensor(seq_lens, "seq_lens", at::kInt);
+  TORCH_CHECK(q.dim() == 3, "q must have shape [B, Hq, D]");
+  TORCH_CHECK(k_pages.dim() == 4, "k_pages must have shape [num_pages, Hkv, page_size, D]");
+  TORCH_CHECK(v_pages.sizes() == k_pages.sizes(), "v_pages must have the shape of k_pages");
+  const int64_t B = q.size(0), Hq = q.size(1), D = q.size(2);
+  TORCH_CHECK(block_table.dim() == 2 && block_table.size(0) == B, "block_table must have shape [B, max_pages]");
+  TORCH_CHECK(seq_lens.dim() == 1 && seq_lens.size(0) == B, "seq_lens must have shape [B]");
+  for (const auto* t : {&k_pages, &v_pages, &block_table, &seq_lens})
+    TORCH_CHECK(t->device() == q.device(), "all tensors must be on q's device");
+  TORCH_CHECK(k_pages.size(3) == D, "k_pages must have shape [num_pages, Hkv, page_size, D]");
+  TORCH_CHECK(k_pages.size(0) <= INT32_MAX && max_seq_len <= INT32_MAX && max_seq_len >= 1, "unsupported size");
+  const double sc = scale.has_value() ? *scale : 1.0 / std::sqrt((double)D);
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto o = torch::empty({B, Hq, D}, q.options());
+  const cudaStream_t stream = current_stream();
+  const int Hkv = (int)k_pages.size(1);
+  const size_t ws_bytes = focal_gqa_decode_workspace_size((int)B, (int)Hq, Hkv, (int)max_seq_len, (int)D);
+  void* ws = nullptr;
+  torch::Tensor ws_t;
+  if (ws_bytes > 0) {
+    ws_t = workspace_for(kWsAttention, q.device(), stream, ws_bytes);
+    ws = ws_t.data_ptr();
+  }
+  raise_on(focal_gqa_decode_paged(q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
+                                  block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(), o.data_ptr(),
+                                  (int)B, (int)Hq, Hkv, (int)D, (int)k_pages.size(0), (int)k_pages.size(2),
+                                  (int)block_table.size(1), (int)max_seq_len, (float)sc, ws, ws_bytes, stream));
+  return o;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -275,6 +312,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_gate_up_silu_tiled", &w4a16_gate_up_silu_tiled, "fused gate/up/SiLU on unit-tiled weights");
   m.def("dequant", &dequant, "fp32 dequantized weights (bit-identical to dequant_ref)");
   m.def("pack_int4", &pack_int4, "pack uint8 [N,K] nibbles into int32 [N,K/8]");
+  m.def("gqa_decode_attention_paged", &gqa_decode_attention_paged, "paged variable-length GQA decode attention",
+        pybind11::arg("q"), pybind11::arg("k_pages"), pybind11::arg("v_pages"), pybind11::arg("block_table"),
+        pybind11::arg("seq_lens"), pybind11::arg("max_seq_len"), pybind11::arg("scale") = pybind11::none());
   m.def("gqa_decode_attention", &gqa_decode_attention, "contiguous GQA decode attention",
         pybind11::arg("q"), pybind11::arg("k_cache"), pybind11::arg("v_cache"),
         pybind11::arg("scale") = pybind11::none());

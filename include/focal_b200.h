@@ -231,9 +231,27 @@ int focal_gqa_decode_attn(const void* q, const void* k, const void* v, void* o, 
                           int Hkv, int L, int D, float scale, void* workspace, size_t ws_bytes,
                           cudaStream_t stream);
 
+/* Paged (variable-length) form, new as well: the caches are pages shared by
+ * all sequences, k_pages / v_pages bf16 [num_pages, Hkv, page_size, D]; page j
+ * of sequence b is block_table[b * max_pages_per_seq + j] (int32), and
+ * sequence b has seq_lens[b] positions (int32, 1 .. max_seq_len; entries of
+ * the block table past a sequence's last page are not read).  page_size is
+ * 16, 32 or a multiple of 64; max_seq_len <= max_pages_per_seq * page_size.
+ * Workspace: focal_gqa_decode_workspace_size(B, Hq, Hkv, max_seq_len, D)
+ * bytes, same rules as above.  A page id or length out of range sets device
+ * status 3 and is clamped (the output is then not meaningful).  With every
+ * seq_lens[b] == max_seq_len and the pages holding the contiguous caches, the
+ * result is bit-identical to focal_gqa_decode_attn's. */
+int focal_gqa_decode_paged(const void* q, const void* k_pages, const void* v_pages, const int32_t* block_table,
+                           const int32_t* seq_lens, void* o, int B, int Hq, int Hkv, int D, int num_pages,
+                           int page_size, int max_pages_per_seq, int max_seq_len, float scale, void* workspace,
+                           size_t ws_bytes, cudaStream_t stream);
+
 /* ------------------------------------------------------------ diagnostics ---
  * Device-side status word of the current device: 0 while every kernel's
- * bounded waits have completed; a nonzero focal device status otherwise.
+ * bounded waits have completed; otherwise 1 (a pipeline wait gave up), 2 (a
+ * tensor-parallel peer did not deliver in time) or 3 (a paged-KV page id or
+ * sequence length out of range).
  * Synchronous (reads device memory).  focal_reset_device_status clears it. */
 int focal_device_status(int* status_out);
 int focal_reset_device_status(void);

@@ -49,3 +49,26 @@ def random_case(B: int, Hq: int, Hkv: int, L: int, D: int, seed: int):
     k = f32_to_bf16(rng.standard_normal((B, Hkv, L, D), dtype=np.float32))
     v = f32_to_bf16(rng.standard_normal((B, Hkv, L, D), dtype=np.float32))
     return q, k, v
+
+
+def paged_to_contiguous(pages: np.ndarray, block_table: np.ndarray, b: int, L: int) -> np.ndarray:
+    """Sequence b's first L positions gathered from pages [num_pages, Hkv,
+    page_size, D] through its block-table row: [Hkv, L, D]."""
+    page_size = pages.shape[2]
+    n = (L + page_size - 1) // page_size
+    seq = np.concatenate([pages[block_table[b, j]] for j in range(n)], axis=1)
+    return seq[:, :L]
+
+
+def decode_attention_paged(q_bf16: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarray,
+                           block_table: np.ndarray, seq_lens: np.ndarray, scale: float | None = None) -> np.ndarray:
+    """Paged, variable-length decode attention: each sequence b attends over its
+    own seq_lens[b] positions, read page by page through its block-table row
+    (the same mathematics as decode_attention, one sequence at a time)."""
+    out = []
+    for b in range(q_bf16.shape[0]):
+        L = int(seq_lens[b])
+        k = paged_to_contiguous(k_pages, block_table, b, L)[None]
+        v = paged_to_contiguous(v_pages, block_table, b, L)[None]
+        out.append(decode_attention(q_bf16[b:b + 1], k, v, scale)[0])
+    return np.stack(out)

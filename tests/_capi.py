@@ -118,3 +118,18 @@ def gate_up_silu_tiled(x, tiles_gate, tiles_up, N):
     _lib.call("focal_w4a16_gate_up_silu_tiled", ptr(x), ptr(tiles_gate), ptr(tiles_up), ptr(h), M, K, N,
               ptr(buf), n, stream_ptr())
     return h
+
+
+def paged_attention(q, k_pages, v_pages, block_table, seq_lens, max_seq_len, scale=None, ws=None):
+    B, Hq, D = q.shape
+    num_pages, Hkv, page_size = k_pages.shape[0], k_pages.shape[1], k_pages.shape[2]
+    if scale is None:
+        scale = 1.0 / np.sqrt(D)
+    if ws is None:
+        ws = attention_workspace(B, Hq, Hkv, max_seq_len, D, q.device)
+    buf, n = ws
+    o = torch.empty_like(q)
+    _lib.call("focal_gqa_decode_paged", ptr(q), ptr(k_pages), ptr(v_pages), ptr(block_table), ptr(seq_lens),
+              ptr(o), B, Hq, Hkv, D, num_pages, page_size, block_table.shape[1], max_seq_len, float(scale),
+              ptr(buf), n, stream_ptr())
+    return o

@@ -101,3 +101,19 @@ def test_tp_buffer_sizing_and_argument_errors():
     rc = L.focal_w4a16_gemv_allreduce(None, None, None, None, None, 8, 4096, 4096, ctypes.byref(comm),
                                       None, 0, None)
     assert rc == _lib.FOCAL_ERR_INVALID_VALUE and "rank 0 is null" in _lib.last_error()
+
+
+def test_paged_attention_argument_errors_without_gpu():
+    L = _lib.lib()
+    args = dict(B=2, Hq=32, Hkv=8, D=128, num_pages=16, page_size=24, max_pages=8, max_len=128)
+
+    def call(**kw):
+        a = dict(args, **kw)
+        return L.focal_gqa_decode_paged(None, None, None, None, None, None, a["B"], a["Hq"], a["Hkv"], a["D"],
+                                        a["num_pages"], a["page_size"], a["max_pages"], a["max_len"], 0.1,
+                                        None, 0, None)
+
+    assert call() == _lib.FOCAL_ERR_UNSUPPORTED and "page_size" in _lib.last_error()
+    assert call(page_size=16, max_pages=4) == _lib.FOCAL_ERR_UNSUPPORTED and "max_seq_len" in _lib.last_error()
+    assert call(page_size=64, D=64) == _lib.FOCAL_ERR_UNSUPPORTED and "head_dim" in _lib.last_error()
+    assert call(page_size=128) == _lib.FOCAL_ERR_INVALID_VALUE and "null" in _lib.last_error()
