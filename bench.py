@@ -581,7 +581,8 @@ def run_tp70b(args, rank, world, local):
 
 def run_profile_case(args):
     """A few calls of one shape, for ncu captures of a single kernel:
-    --profile-shape M,K,N (W4A16) or --profile-attn B,L (attention)."""
+    --profile-shape M,K,N (W4A16), --profile-attn B,L (attention) or
+    --profile-paged B,L,page_size (paged attention, pages shuffled)."""
     import torch
 
     import focal_b200 as F
@@ -595,6 +596,16 @@ def run_profile_case(args):
         M, K, N = (int(v) for v in args.profile_shape.split(","))
         case = F.baseline_case(M, K, N, seed=1, device=dev)
         fn = lambda: F.w4a16_linear(*case)  # noqa: E731
+    elif args.profile_paged:
+        B, L, ps = (int(v) for v in args.profile_paged.split(","))
+        g = torch.Generator(device="cpu").manual_seed(1)
+        per = (L + ps - 1) // ps
+        q = torch.randn((B, 32, 128), generator=g).to(torch.bfloat16).to(dev)
+        kp = torch.randn((B * per, 8, ps, 128), generator=g).to(torch.bfloat16).to(dev)
+        vp = torch.randn((B * per, 8, ps, 128), generator=g).to(torch.bfloat16).to(dev)
+        table = torch.randperm(B * per, generator=g).to(torch.int32).view(B, per).to(dev)
+        lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+        fn = lambda: F.gqa_decode_attention_paged(q, kp, vp, table, lens, L)  # noqa: E731
     else:
         B, L = (int(v) for v in args.profile_attn.split(","))
         g = torch.Generator(device="cpu").manual_seed(1)
@@ -620,10 +631,11 @@ def main(argv=None):
     ap.add_argument("--no-secondary", action="store_true", help="skip the attention shapes")
     ap.add_argument("--profile-shape", default=None, help="M,K,N: only run a few calls (ncu)")
     ap.add_argument("--profile-attn", default=None, help="B,L: only run a few attention calls (ncu)")
+    ap.add_argument("--profile-paged", default=None, help="B,L,page_size: a few paged attention calls (ncu)")
     ap.add_argument("--profile-sweep", action="store_true", help="each sweep shape once per call round (ncu)")
     ap.add_argument("--profile-calls", type=int, default=3)
     args = ap.parse_args(argv)
-    if args.profile_shape or args.profile_attn or args.profile_sweep:
+    if args.profile_shape or args.profile_attn or args.profile_sweep or args.profile_paged:
         run_profile_case(args)
         return 0
     if args.warmup < 3:
