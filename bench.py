@@ -569,7 +569,7 @@ def run_tp70b(args, rank, world, local):
             "config": {"workload": "tp70b_decode_layer", "M": M, "column": [K1, N1], "row": [K2, N2],
                        "parallelism": f"tp{world}",
                        "collectives": "bf16 all-gather + fp32 all-reduce inside the two GEMV kernels "
-                                      "(peer-memory stores over NVLink, epoch flags)",
+                                      "(64-bit {value, epoch} stores to peer memory over NVLink)",
                        "l2": f"cold: {copies} rotating weight copies per rank"},
             "kernel_only": {"value": round(world * per_rank / (ms_k * 1e-3) / 1e9, 2), "unit": "GB/s",
                             "ms_per_step": round(ms_k, 5),
