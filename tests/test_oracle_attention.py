@@ -24,3 +24,31 @@ def test_oracle_single_position_returns_v():
     q, k, v = oa.random_case(1, 4, 1, 1, 128, seed=3)
     o = oa.decode_attention(q, k, v)
     assert np.array_equal(o, np.repeat(v[:, :, 0, :], 4, axis=1))
+
+
+def _pages(k, page_size, seed):
+    """Scatter k [B, Hkv, L, D] into shuffled pages; return (pages, block table)."""
+    B, Hkv, L, D = k.shape
+    per = -(-L // page_size)
+    order = np.random.default_rng(seed).permutation(B * per + 2)
+    pages = np.zeros((B * per + 2, Hkv, page_size, D), dtype=k.dtype)
+    table = np.zeros((B, per), dtype=np.int32)
+    for b in range(B):
+        for j in range(per):
+            rows = min(page_size, L - j * page_size)
+            pages[order[b * per + j], :, :rows] = k[b, :, j * page_size: j * page_size + rows]
+            table[b, j] = order[b * per + j]
+    return pages, table
+
+
+@pytest.mark.parametrize("page_size", [16, 64])
+def test_paged_oracle_equals_contiguous(page_size):
+    q, k, v = oa.random_case(3, 8, 2, 100, 128, seed=page_size)
+    kp, table = _pages(k, page_size, seed=1)
+    vp, _ = _pages(v, page_size, seed=1)
+    full = oa.decode_attention_paged(q, kp, vp, table, np.array([100, 100, 100]))
+    assert np.array_equal(full, oa.decode_attention(q, k, v))
+    ragged = oa.decode_attention_paged(q, kp, vp, table, np.array([1, 37, 100]))
+    for b, L in enumerate((1, 37, 100)):
+        want = oa.decode_attention(q[b:b + 1], k[b:b + 1, :, :L], v[b:b + 1, :, :L])
+        assert np.array_equal(ragged[b:b + 1], want)
