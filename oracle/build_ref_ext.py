@@ -8,10 +8,11 @@ the reference's build system) so that its kernel can be timed on a B200 beside
 focal_b200's.  The output is a plain torch extension module that exports the
 reference's ``w4a16_linear(x, wq, scales, zeros)``.
 
-    python oracle/build_ref_ext.py [REFERENCE_ROOT]
+    FOCAL_REFERENCE_DIR=<reference checkout> python oracle/build_ref_ext.py
+    python oracle/build_ref_ext.py <reference checkout>
 
-REFERENCE_ROOT defaults to /root/reference (the reference checkout in the build
-container; it does not exist on the GPU machines, which use the built .so).
+The checkout is given explicitly (argument or FOCAL_REFERENCE_DIR; there is no
+default location).  The GPU machines do not have it and use the built .so.
 """
 from __future__ import annotations
 
@@ -24,7 +25,7 @@ OUT = HERE / "_ref"
 NAME = "focal_w4a16_ref_C"
 
 
-def build(ref_root: str = "/root/reference") -> Path:
+def build(ref_root: str) -> Path:
     from torch.utils.cpp_extension import load
 
     src = Path(ref_root) / "csrc"
@@ -47,4 +48,9 @@ def load_built():
 
 
 if __name__ == "__main__":
-    print(build(*sys.argv[1:]))
+    import os
+
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FOCAL_REFERENCE_DIR")
+    if not root:
+        sys.exit("give the reference checkout as an argument or in FOCAL_REFERENCE_DIR")
+    print(build(root))

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this folder from the reference's own code.
 
-Run once, in a container that has the reference checkout (default path
-``/root/reference``; override with FOCAL_REFERENCE_DIR):
+Run once, in a container that has the reference checkout, naming it in
+FOCAL_REFERENCE_DIR (there is no default location):
 
-    python tests/golden/make_golden.py
+    FOCAL_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference package ``focal_w4a16`` from that checkout, relaxes
 its CUDA-only guard (``require_cuda_contiguous``, focal_w4a16/__init__.py:31-35)
@@ -34,10 +34,12 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF_DIR = Path(os.environ.get("FOCAL_REFERENCE_DIR", "/root/reference"))
+REF_DIR = Path(os.environ["FOCAL_REFERENCE_DIR"]) if os.environ.get("FOCAL_REFERENCE_DIR") else None
 
 
 def load_reference():
+    if REF_DIR is None or not (REF_DIR / "focal_w4a16").is_dir():
+        sys.exit("FOCAL_REFERENCE_DIR must name the reference checkout (with focal_w4a16/)")
     sys.path.insert(0, str(REF_DIR))
     try:
         ref = importlib.import_module("focal_w4a16")

@@ -88,3 +88,16 @@ def test_bf16_round_trip_and_rounding():
     b = ow.f32_to_bf16(vals)
     # ties go to even: 1 + 2^-8 -> 1.0, 1 + 3*2^-8 -> 1 + 2^-6
     assert list(ow.bf16_to_f32(b)) == [1.0, 1.0, 1.0 + 2**-6, -2.5, 0.0, np.inf]
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 4096), (8, 4096, 11008), (4, 11008, 4096), (2, 8192, 8192)])
+def test_threaded_cpu_baseline_matches_pinned_linear(M, K, N):
+    """The timed CPU baseline (linear_threaded, which bench.py's cpu_baseline leg
+    and --impl reference time) equals the fixture-pinned oracle linear to within
+    one bf16 ulp per element: the same fp32 dequant and accumulation, only the
+    BLAS blocking differs."""
+    x, wq, s, z = ow.baseline_case(M, K, N, seed=77 + M)
+    a = ow.bf16_to_f32(ow.linear_threaded(x, wq, s, z, threads=4)).astype(np.float64)
+    b = ow.bf16_to_f32(ow.linear(x, wq, s, z)).astype(np.float64)
+    ulp = np.abs(b) * 2.0 ** -7 + 1e-30  # one bf16 ulp (8 significant bits) at |b|
+    assert np.all(np.abs(a - b) <= ulp), float(np.max(np.abs(a - b) / ulp))
