@@ -77,6 +77,32 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
   }
 }
 
+// Non-blocking test of phase `parity` (never suspends the warp).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait that polls without suspending, for warps on the critical path.
+__device__ __forceinline__ bool mbar_wait_bounded_spin(uint32_t bar, uint32_t parity) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      if (mbar_test_wait(bar, parity)) return true;
+    }
+    if (clock64() - t0 > kWaitLimitCycles) return false;
+  }
+}
+
 // -------------------------------------------------------------------- TMA
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t pol;

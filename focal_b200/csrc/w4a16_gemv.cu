@@ -19,7 +19,7 @@
 //      TMA box of 64 rows x 128 bytes (128-byte swizzle), the fp16 scales and
 //      zeros (below), and the unit's activation record, which the warp builds
 //      itself from x (the tensor core's B fragments for the unit's 256 K
-//      values plus fp32 sums per 128-wide group).  Scales and zeros:
+//      values).  Scales and zeros:
 //      when K % 1024 == 0, one 2-D TMA box each of 64 rows x 8 groups per
 //      four units (a "quad", two quad slots per sub-pipeline), otherwise the
 //      unit's two groups per row with 4-byte cp.async.  All complete on the
@@ -34,7 +34,9 @@
 //      mma.sync m16n8k16 (bf16 in, fp32 accumulate); the <= 8 tokens are the
 //      n = 8 side.  Zero point and +128 factor out per group:
 //          sum_k x (q - z) s = s * (sum_k x (128 + q) - (z + 128) sum_k x)
-//      so the tensor core only sees exact small integers and x.
+//      so the tensor core only sees exact small integers and x.  The group
+//      sums of x come from the tensor core too: one extra MMA per k step with
+//      an A operand of ones (bf16 1.0), sharing the B fragments.
 //    * at the end of each row block's run in a range the two warps' shares
 //      are added (group 0 then group 1) and the sub-pipeline either writes y
 //      (its range held the whole row block), or, when the CTA's four ranges
@@ -64,7 +66,11 @@ constexpr int kRows = 16 * kRowTiles;   // weight rows per unit
 // sub-pipeline p has producer warp 8 + p, a ring of ring_of(NW) slots and
 // consumer warps 2p, 2p + 1 (one per quantisation group of a unit).
 constexpr int kPairs = 4;
-constexpr int kConsumerWarps = 2 * kPairs;
+constexpr int kCW = 2;
+#define FOCAL_GEMV_MAXNREG 160
+constexpr int kTPW = kRowTiles * 2 / kCW;  // 16-row tiles per consumer warp
+constexpr int kPairThreads = 32 * kCW;
+constexpr int kConsumerWarps = kCW * kPairs;
 constexpr int kThreads = 32 * (kConsumerWarps + kPairs);
 // One resident CTA per SM (12 warps at up to 160 registers): 12 x 8 KB (gate/up:
 // 8 x 16 KB) of weights in flight.
@@ -118,15 +124,12 @@ struct TpParams {
 };
 
 // ---------------------------------------------------- activation records
-// One record per unit column: [group G][token m][t][4 x 16 B] B fragments, then
-// the fp32 group sums [G][MTp].  The fragment of lane 4g+t for chunk qq holds
+// One record per unit column: [group G][token m][t][4 x 16 B] B fragments.  The fragment of lane 4g+t for chunk qq holds
 // the pairs (x_j, x_{j+4}), j = 0..3, of K values 128G + 32t + 8qq + j, matching
 // the nibble pairs (q_j, q_{j+4}) that one packed word yields.
 __host__ __device__ constexpr int mtp_of(int MT) { return MT < 2 ? 2 : MT; }
 __host__ __device__ constexpr uint32_t rec_frag_bytes(int MT) { return MT * 2 * 256; }
-__host__ __device__ constexpr uint32_t rec_bytes(int MT) {
-  return rec_frag_bytes(MT) + ((2 * mtp_of(MT) * 4 + 15) / 16) * 16;
-}
+__host__ __device__ constexpr uint32_t rec_bytes(int MT) { return rec_frag_bytes(MT); }
 
 // Byte offset of chunk qq of lane (g, t), group G, inside a record.  Rotating
 // a lane's four chunks by (lane >> 1) keeps each 8-lane LDS.128 phase
@@ -176,7 +179,7 @@ struct Params {
 };
 
 struct Layout {
-  uint32_t w, x, sz, red, flag, bars, total;
+  uint32_t w, x, sz, red, flag, bars, tl, total;
 };
 
 __host__ __device__ constexpr uint32_t round_up(uint32_t a, uint32_t b) { return (a + b - 1) / b * b; }
@@ -204,6 +207,10 @@ __host__ __device__ constexpr Layout make_layout() {
   off += 32;
   L.bars = round_up(off, 8);  // full[slots], empty[slots]
   off = L.bars + 2 * slots * 8;
+#ifdef FOCAL_TIMELINE
+  L.tl = round_up(off, 16);
+  if (NW == 1) off = L.tl + kPairs * 64 * 8 * 4;
+#endif
   L.total = off + 1024;  // slack for aligning the base to 1024 B
   return L;
 }
@@ -342,8 +349,33 @@ __device__ __forceinline__ void tp_complete(const Params& p, int rb, int ptid, u
   }
 }
 
+#ifdef FOCAL_TIMELINE
+constexpr int kTlCtas = 160, kTlUnits = 64;
+__device__ long long* g_tl;
+__device__ __forceinline__ long long gtimer() {
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// stamps go to shared memory (uint32 cycles since the CTA's start) and are
+// copied out at the end, so they add no global stores to the timed loop
+#define TL(ev, j)                                                                                        \
+  do {                                                                                                   \
+    if (NW == 1 && (j) < kTlUnits)                                                                               \
+      reinterpret_cast<volatile uint32_t*>(sm + L.tl)[(pair * kTlUnits + (j)) * 8 + (ev)] =              \
+          (uint32_t)(clock64() - tl_t0);                                                                 \
+  } while (0)
+#define TLH(i, v)                                                                                         \
+  do {                                                                                                    \
+    if (g_tl && blockIdx.x < kTlCtas) g_tl[(size_t)kTlCtas * kPairs * kTlUnits * 8 + blockIdx.x * 8 + (i)] = (v); \
+  } while (0)
+#else
+#define TL(ev, j)
+#define TLH(i, v)
+#endif
+
 template <int MT, int NW, int EPI>
-__global__ void __maxnreg__(160)
+__global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     w4a16_gemv_kernel(const __grid_constant__ CUtensorMap tmap0, const __grid_constant__ CUtensorMap tmap1,
                       const __grid_constant__ CUtensorMap tms0, const __grid_constant__ CUtensorMap tmz0,
                       const __grid_constant__ CUtensorMap tms1, const __grid_constant__ CUtensorMap tmz1,
@@ -362,13 +394,22 @@ __global__ void __maxnreg__(160)
   const int lane = threadIdx.x & 31;
   // this warp's sub-pipeline and its range of units (p.P ranges in all; a
   // sub-pipeline of the last CTA may have none)
-  const int pair = warp < kConsumerWarps ? (warp >> 1) : (warp - kConsumerWarps);
+  const int pair = warp < kConsumerWarps ? (warp / kCW) : (warp - kConsumerWarps);
   const int vc = blockIdx.x * kPairs + pair;
   const long long u0 = vc < p.P ? unit_begin(vc, p.U, p.P) : 0;
   const long long u1 = vc < p.P ? unit_begin(vc + 1, p.U, p.P) : 0;
   const int nu = (int)(u1 - u0);
   const int rb0 = (int)(u0 / p.TS), st0 = (int)(u0 - (long long)rb0 * p.TS);
 
+#ifdef FOCAL_TIMELINE
+  const long long tl_t0 = clock64();
+  if (threadIdx.x == 0) {
+    TLH(0, tl_t0);
+    TLH(1, gtimer());
+  }
+  if (NW == 1)
+    for (int i = threadIdx.x; i < kPairs * kTlUnits * 8; i += blockDim.x) reinterpret_cast<uint32_t*>(sm + L.tl)[i] = 0u;
+#endif
   const uint32_t full_bar = base + L.bars;
   const uint32_t empty_bar = full_bar + kSlots * 8;
 
@@ -378,7 +419,7 @@ __global__ void __maxnreg__(160)
       // the producer's expect_tx and its activation-record arrival, plus 32
       // cp.async arrivals when scales / zeros use cp.async
       mbar_init(full_bar + 8 * s, (p.sz_tma || p.tiles0) ? 2 : 2 + 32);
-      mbar_init(empty_bar + 8 * s, 2);  // the sub-pipeline's two consumer warps
+      mbar_init(empty_bar + 8 * s, kCW);  // the sub-pipeline's consumer warps
     }
     *reinterpret_cast<unsigned int*>(sm + L.flag + 16) = 0u;  // in-CTA row-block arrivals
     fence_barrier_init();
@@ -411,6 +452,7 @@ __global__ void __maxnreg__(160)
     // boxes) of local unit j, on its slot's full barrier; the activation
     // record is written separately.
     auto issue_unit = [&](int j, int rb, int st, bool opens_quad, int qs) {
+      TL(0, j);
       const int slot = pp * R + j % R;
       const uint32_t fb = full_bar + 8 * slot;
       if (p.tiles0) {
@@ -458,9 +500,12 @@ __global__ void __maxnreg__(160)
       }
     }
     griddep_wait();  // x may be the previous kernel's output
+#ifdef FOCAL_TIMELINE
+    if (pp == 0 && lane == 0) TLH(4, clock64());
+#endif
     // Activation record of stage st, written by the warp into the slot: for
-    // each token m the B fragments of K values 256st + 8l .. 8l + 7 (lane l),
-    // then the fp32 sums of the two 128-wide groups.  x is a few KB to a few
+    // each token m the B fragments of K values 256st + 8l .. 8l + 7 (lane l).
+    // x is a few KB to a few
     // hundred KB and shared by every CTA, so these loads hit L2; each unit's
     // slice is loaded one unit ahead so their latency stays off the ring.
     auto load_x = [&](uint4 (&v)[MTp], int st) {
@@ -475,13 +520,6 @@ __global__ void __maxnreg__(160)
       const int Gq = lane >> 4, c = lane & 15;
 #pragma unroll
       for (int m = 0; m < MTp; ++m) {
-        float sum = bf16_lo(v[m].x) + bf16_hi(v[m].x) + bf16_lo(v[m].y) + bf16_hi(v[m].y) + bf16_lo(v[m].z) +
-                    bf16_hi(v[m].z) + bf16_lo(v[m].w) + bf16_hi(v[m].w);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-        if (c == 0) reinterpret_cast<float*>(rec + rec_frag_bytes(MT))[Gq * MTp + m] = sum;
         if (m < MT) {
           uint4 pv;
           pv.x = prmt(v[m].x, v[m].z, 0x5410);
@@ -514,7 +552,10 @@ __global__ void __maxnreg__(160)
           if (j + 1 < nu) load_x(xnext, st + 1 == p.TS ? 0 : st + 1);
           write_record(sm + L.x + slot * kRec, xcur);
           __syncwarp();
-          if (lane == 0) mbar_arrive(fb);  // the record's arrival (release: orders the writes above)
+          if (lane == 0) {
+            TL(1, j);
+            mbar_arrive(fb);  // the record's arrival (release: orders the writes above)
+          }
 #pragma unroll
           for (int m = 0; m < MTp; ++m) xcur[m] = xnext[m];
           if (!p.sz_tma && !p.tiles0) {
@@ -546,37 +587,35 @@ __global__ void __maxnreg__(160)
     const int tid = threadIdx.x;  // 0 .. kConsumerThreads-1
     const int g = lane >> 2, t = lane & 3;
     const int G = warp & 1;  // which quantisation group of its units this warp takes
-    const int ptid = tid & 63;  // thread index within the pair
+    const int ptid = tid % kPairThreads;  // thread index within the pair
     // Lane (g, t) covers rows pg + 8h, h = 0..7 (tile h/2, MMA row g or g+8): the
     // permutation keeps the swizzled reads conflict-free, and because every such
     // row is pg mod 8 the 128-byte swizzle maps chunk 4G+t to one column for all.
     const int pg = (g >> 1) + ((g & 1) << 2);
     const bool has_token = g < p.M;
     const int gc = g < MT ? g : 0;
-    const int tok2 = 2 * t < MTp ? 2 * t : 0;
     const uint32_t kMask = 0x000F000Fu, kMagic = 0x43004300u;  // held in registers
     const uint32_t w_lane = L.w + pg * 128 + ((uint32_t)((4 * G + t) ^ pg) << 4);
     uint32_t x_off[4];
 #pragma unroll
     for (int qq = 0; qq < 4; ++qq) x_off[qq] = L.x + frag_offset(MT, G, gc, t, qq);
-    const uint32_t xs_off = L.x + rec_frag_bytes(MT) + (G * MTp + tok2) * 4;
     // scale/zero staging: 16-byte rows (quad slots) or 4-byte rows (ring slots)
     const uint32_t rs = p.sz_tma ? 16u : 4u;
     const uint32_t sz_mat = 2 * kRows * rs;  // bytes per (slot, mat)
     const uint32_t sz_lane = L.sz + pg * rs;
     const int half_shift = 16 * G;  // this group's fp16 within a scale/zero pair
-    float acc[NW][kRowTiles][4];
+    float acc[NW][kTPW][4];
 #pragma unroll
     for (int mat = 0; mat < NW; ++mat)
 #pragma unroll
-      for (int tl = 0; tl < kRowTiles; ++tl)
+      for (int tl = 0; tl < kTPW; ++tl)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[mat][tl][j] = 0.f;
 
     int pend_rb = -1;  // tensor-parallel: a row block this pair sent but has not completed
     auto finished = [&](int frb) {
       if constexpr (is_tp(EPI)) {
-        if (pend_rb >= 0) tp_complete<MT, EPI>(p, pend_rb, ptid, tp_e);
+        if (pend_rb >= 0 && ptid < kRows) tp_complete<MT, EPI>(p, pend_rb, ptid, tp_e);
         pend_rb = frb;
       }
     };
@@ -589,7 +628,15 @@ __global__ void __maxnreg__(160)
         // After a wait gives up, later waits are skipped (the result is garbage
         // and the status word is set) but every warp still takes the same path
         // through the row-block barriers below, so none of them can hang.
-        if (ok && !mbar_wait_bounded(full_bar + 8 * slot, (j / R) & 1)) ok = false;
+#ifdef FOCAL_TIMELINE
+        if (warp % kCW == 0 && lane == 0) TL(4, j);
+#endif
+        // (polled without suspending: the slot is usually full already, and a
+        // suspended warp wakes late)
+        if (ok && !mbar_wait_bounded_spin(full_bar + 8 * slot, (j / R) & 1)) ok = false;
+#ifdef FOCAL_TIMELINE
+        if (warp % kCW == 0 && lane == 0) TL(2, j);
+#endif
         const uint32_t xso = slot * kRec;                // this slot's activation record
         const uint32_t wso = slot * (NW * kRows * 128);  // this slot's weight boxes
         // B fragments: token g, K values 128G + 32t + 8qq + {j, j+4}
@@ -597,14 +644,22 @@ __global__ void __maxnreg__(160)
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
           uint4 v = make_uint4(0u, 0u, 0u, 0u);
-          if (has_token) v = ld_smem<uint4>(sm, x_off[qq] + xso);
+          if (has_token) v = lds128(base + x_off[qq] + xso);
           xb[4 * qq + 0] = v.x;
           xb[4 * qq + 1] = v.y;
           xb[4 * qq + 2] = v.z;
           xb[4 * qq + 3] = v.w;
         }
         // group sums of x for tokens 2t and 2t+1
-        const float2 xs = ld_smem<float2>(sm, xs_off + xso);
+        float2 xs;
+        {
+          float ds[4] = {0.f, 0.f, 0.f, 0.f};
+          const uint32_t one = 0x3F803F80u;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) mma_bf16_16816(ds, one, one, one, one, xb[2 * kk], xb[2 * kk + 1]);
+          xs.x = ds[0];
+          xs.y = ds[1];
+        }
         const uint32_t sz_slot = p.sz_tma ? (uint32_t)(pair * kSzQuadSlots + qs) : (uint32_t)slot;
         const uint32_t sz_col = p.sz_tma ? (uint32_t)(st & 3) * 4u : 0u;
 #pragma unroll
@@ -613,29 +668,32 @@ __global__ void __maxnreg__(160)
           const uint32_t wb = w_lane + wso + mat * kRows * 128;
           // every load of the unit first (one shared-memory latency), then the
           // four tiles' MMA chains interleaved
-          uint4 wv[kRowTiles][2];
-          uint32_t sv[kRowTiles][2], zv[kRowTiles][2];
+          uint4 wv[kTPW][2];
+          uint32_t sv[kTPW][2], zv[kTPW][2];
 #pragma unroll
-          for (int tl = 0; tl < kRowTiles; ++tl) {
+          for (int tl = 0; tl < kTPW; ++tl) {
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
               const uint32_t r = 16 * tl + 8 * hf;  // rows beyond pg
-              wv[tl][hf] = ld_smem<uint4>(sm, wb + r * 128);
-              sv[tl][hf] = ld_smem<uint32_t>(sm, sb + r * rs) >> half_shift;
-              zv[tl][hf] = ld_smem<uint32_t>(sm, sb + (kRows + r) * rs) >> half_shift;
+              wv[tl][hf] = lds128(base + wb + r * 128);
+              sv[tl][hf] = lds32(base + sb + r * rs) >> half_shift;
+              zv[tl][hf] = lds32(base + sb + (kRows + r) * rs) >> half_shift;
             }
           }
-          float d[kRowTiles][4];
+          float d[kTPW][4];
 #pragma unroll
-          for (int tl = 0; tl < kRowTiles; ++tl)
+          for (int tl = 0; tl < kTPW; ++tl)
 #pragma unroll
             for (int e = 0; e < 4; ++e) d[tl][e] = 0.f;
+#ifdef FOCAL_TIMELINE
+          if (warp % kCW == 0 && lane == 0) TL(5, j);
+#endif
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
 #pragma unroll
-              for (int tl = 0; tl < kRowTiles; ++tl) {
+              for (int tl = 0; tl < kTPW; ++tl) {
                 const uint32_t wa = qq == 0 ? wv[tl][0].x : qq == 1 ? wv[tl][0].y : qq == 2 ? wv[tl][0].z : wv[tl][0].w;
                 const uint32_t wr = qq == 0 ? wv[tl][1].x : qq == 1 ? wv[tl][1].y : qq == 2 ? wv[tl][1].z : wv[tl][1].w;
                 mma_bf16_16816(d[tl], nib_pair_bf16(wa, 2 * h, kMask, kMagic), nib_pair_bf16(wr, 2 * h, kMask, kMagic),
@@ -645,8 +703,11 @@ __global__ void __maxnreg__(160)
               }
             }
           }
+#ifdef FOCAL_TIMELINE
+          if (warp % kCW == 0 && lane == 0) TL(6, j);
+#endif
 #pragma unroll
-          for (int tl = 0; tl < kRowTiles; ++tl) {
+          for (int tl = 0; tl < kTPW; ++tl) {
             const float s0 = half_lo(sv[tl][0]), s1 = half_lo(sv[tl][1]);
             const float z0 = half_lo(zv[tl][0]) + 128.0f, z1 = half_lo(zv[tl][1]) + 128.0f;
             acc[mat][tl][0] = fmaf(s0, fmaf(-z0, xs.x, d[tl][0]), acc[mat][tl][0]);
@@ -657,11 +718,18 @@ __global__ void __maxnreg__(160)
         }
         fence_proxy_async_smem();  // our loads of this slot precede its TMA / bulk refill
         __syncwarp();
+#ifdef FOCAL_TIMELINE
+        if (warp % kCW == 0 && lane == 0) TL(3, j);
+        if (warp % kCW == 1 && lane == 0) TL(7, j);
+#endif
         if (lane == 0) mbar_arrive(empty_bar + 8 * slot);
       }
 
       // ------------------------------------------- end of a row-block run
       const bool run_ends = (j + 1 == nu) || (st + 1 == p.TS);
+#ifdef FOCAL_TIMELINE
+      if (run_ends && warp % kCW == 0 && lane == 0) TL(0, 63);
+#endif
       if (run_ends) {
         const int bar = 2 + pair;  // the pair's named barrier (64 threads)
         float* red = reinterpret_cast<float*>(sm + L.red) + pair * NW * MT * kRows;  // [mat][token][row]
@@ -672,7 +740,7 @@ __global__ void __maxnreg__(160)
 #pragma unroll
             for (int mat = 0; mat < NW; ++mat) {
 #pragma unroll
-              for (int tl = 0; tl < kRowTiles; ++tl) {
+              for (int tl = 0; tl < kTPW; ++tl) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const int tok = 2 * t + (e & 1);
@@ -684,18 +752,19 @@ __global__ void __maxnreg__(160)
               }
             }
           }
-          named_barrier(bar, 64);
+          named_barrier(bar, kPairThreads);
         }
         const long long rb_lo = (long long)rb * p.TS, rb_hi = rb_lo + p.TS;
         const int nout = p.M * kRows;
         if (u0 <= rb_lo && u1 >= rb_hi) {
           // the whole row block was this range's
-          finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](float(&v)[MT][NW]) {
+          if (ptid < kRows)
+            finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](float(&v)[MT][NW]) {
 #pragma unroll
-            for (int tok = 0; tok < MT; ++tok)
+              for (int tok = 0; tok < MT; ++tok)
 #pragma unroll
-              for (int mat = 0; mat < NW; ++mat) v[tok][mat] = red[(mat * MT + tok) * kRows + ptid];
-          });
+                for (int mat = 0; mat < NW; ++mat) v[tok][mat] = red[(mat * MT + tok) * kRows + ptid];
+            });
           finished(rb);
         } else if (4 * (int)blockIdx.x + 3 < p.P && rb_lo == unit_begin(4 * blockIdx.x, p.U, p.P) &&
                    rb_hi == unit_begin(4 * blockIdx.x + 4, p.U, p.P)) {
@@ -706,8 +775,8 @@ __global__ void __maxnreg__(160)
           // increment and barrier order its reads after all four.
           int* flag = reinterpret_cast<int*>(sm + L.flag) + pair;
           if (ptid == 0) *flag = (atom_add_acq_rel_cta_shared(base + L.flag + 16, 1u) == kPairs - 1);
-          named_barrier(bar, 64);
-          if (*flag) {
+          named_barrier(bar, kPairThreads);
+          if (*flag && ptid < kRows) {
             finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](float(&v)[MT][NW]) {
 #pragma unroll
               for (int tok = 0; tok < MT; ++tok)
@@ -725,7 +794,7 @@ __global__ void __maxnreg__(160)
         } else {
           // publish this range's partial; the last of the row block's ranges finishes it
           float* mine = p.partials + (2LL * vc + (rb == rb0 ? 0 : 1)) * slot_floats(MT, NW);
-          for (int o = ptid; o < nout; o += 64) {
+          for (int o = ptid; o < nout; o += kPairThreads) {
             const int tok = o / kRows, row = o - tok * kRows;
 #pragma unroll
             for (int mat = 0; mat < NW; ++mat)
@@ -735,18 +804,19 @@ __global__ void __maxnreg__(160)
           // acquire-release increment, which publishes them at GPU scope; in
           // the range that finishes the row block the same increment (acquire)
           // and the barrier after it order the loads of every partial.
-          named_barrier(bar, 64);
+          named_barrier(bar, kPairThreads);
           const int c_first = unit_owner(rb_lo, p.U, p.P), c_last = unit_owner(rb_hi - 1, p.U, p.P);
           int* flag = reinterpret_cast<int*>(sm + L.flag) + pair;
           if (ptid == 0) {
             const unsigned int prev = atom_add_acq_rel_gpu(p.counters + rb, 1u);
             *flag = (prev == (unsigned int)(c_last - c_first));
           }
-          named_barrier(bar, 64);
+          named_barrier(bar, kPairThreads);
           if (*flag) {
             // Partial slots: a range after c_first began inside this row block
             // (slot 2c); c_first used slot 2c + 1 unless it began exactly at rb_lo.
             const long long first_slot = 2LL * c_first + (unit_begin(c_first, p.U, p.P) == rb_lo ? 0 : 1);
+            if (ptid < kRows)
             finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](float(&v)[MT][NW]) {
               // every token's partials of kB ranges loaded together (one L2
               // round trip per batch), added in range order (deterministic)
@@ -781,7 +851,10 @@ __global__ void __maxnreg__(160)
             finished(rb);
           }
         }
-        named_barrier(bar, 64);  // red and the flag are rewritten by the next run
+        named_barrier(bar, kPairThreads);  // red and the flag are rewritten by the next run
+#ifdef FOCAL_TIMELINE
+        if (warp % kCW == 0 && lane == 0) TL(3, 63);
+#endif
       }
       if (++st == p.TS) {
         st = 0;
@@ -789,11 +862,21 @@ __global__ void __maxnreg__(160)
       }
     }
     if constexpr (is_tp(EPI)) {
-      if (pend_rb >= 0) tp_complete<MT, EPI>(p, pend_rb, ptid, tp_e);
+      if (pend_rb >= 0 && ptid < kRows) tp_complete<MT, EPI>(p, pend_rb, ptid, tp_e);
     }
   }
 
   if (!ok && p.status) atomicExch(p.status, kDevWaitTimeout);
+#ifdef FOCAL_TIMELINE
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    TLH(2, clock64());
+    TLH(3, gtimer());
+  }
+  if (NW == 1 && g_tl && blockIdx.x < kTlCtas)
+    for (int i = threadIdx.x; i < kPairs * kTlUnits * 8; i += blockDim.x)
+      g_tl[(size_t)blockIdx.x * kPairs * kTlUnits * 8 + i] = reinterpret_cast<uint32_t*>(sm + L.tl)[i];
+#endif
   if constexpr (is_tp(EPI)) {
     // the last CTA to finish advances this rank's epoch for the next call
     __syncthreads();
@@ -1259,6 +1342,12 @@ int focal_w4a16_gate_up_silu_tiled(const void* x, const void* tiles_gate, const 
   return gemv::run(gemv::kEpiSiluMul, x, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, h, M, K, N,
                    workspace, ws_bytes, stream, nullptr, tiles_gate, tiles_up);
 }
+
+#ifdef FOCAL_TIMELINE
+int focal_tl_set(void* buf) {
+  return cudaMemcpyToSymbol(gemv::g_tl, &buf, sizeof(buf)) == cudaSuccess ? 0 : 4;
+}
+#endif
 
 int focal_w4a16_gemv_noalloc(const void* x, const int32_t* wq, const void* scales, const void* zeros,
                              void* y, int M, int K, int N, cudaStream_t stream) {
