@@ -318,6 +318,10 @@ __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
 // Named barrier over a subset of warps (id 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

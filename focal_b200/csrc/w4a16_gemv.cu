@@ -75,7 +75,8 @@ constexpr int kThreads = 32 * (kConsumerWarps + kPairs);
 // One resident CTA per SM (12 warps at up to 160 registers): 12 x 8 KB (gate/up:
 // 8 x 16 KB) of weights in flight.
 __host__ __device__ constexpr int ring_of(int NW) { return NW == 1 ? 3 : 2; }
-constexpr int kMaxCtasPerSm = 4;        // bound on unit ranges per SM, used to size the workspace
+constexpr int kMaxCtasPerSm = 4;
+constexpr int kMaxCluster = 4;  // CTAs that split one row block's K in cluster split-K mode        // bound on unit ranges per SM, used to size the workspace
 constexpr int kSumBatch = 8;            // partial-sum ranges loaded together by a finisher (MT * NW <= 2)
 constexpr int kMinUnitsPerRange = 4;    // below this, fewer ranges beat more split overhead
 // Scale/zero quad slots per sub-pipeline when they arrive by TMA: the slot of
@@ -172,6 +173,7 @@ struct Params {
   int* status;
   int M, K, N, G, TS, RB, P;
   int sz_tma;   // scales / zeros by TMA quads (needs G % 8 == 0 and 16-byte aligned bases)
+  int csize;    // CTAs per cluster: > 1 splits each row block's K over a cluster (split_k_plan)
   const uint8_t* tiles0;  // unit-tiled weights (w4a16_tiles.h) instead of the maps, when set
   const uint8_t* tiles1;
   TpParams tp;  // tensor-parallel epilogues only
@@ -179,7 +181,7 @@ struct Params {
 };
 
 struct Layout {
-  uint32_t w, x, sz, red, flag, bars, tl, total;
+  uint32_t w, x, sz, red, cred, flag, bars, tl, total;
 };
 
 __host__ __device__ constexpr uint32_t round_up(uint32_t a, uint32_t b) { return (a + b - 1) / b * b; }
@@ -203,6 +205,8 @@ __host__ __device__ constexpr Layout make_layout() {
   off += NW * sz_region_bytes(NW);
   L.red = off;  // [pair][mat][token][64 rows] fp32 shares of the current row block
   off += kPairs * NW * MT * kRows * 4;
+  L.cred = off;  // cluster split-K: [cluster rank][mat][token][64 rows] fp32 CTA sums (leader CTA)
+  off += kMaxCluster * NW * MT * kRows * 4;
   L.flag = off;  // per pair "finish the row block" broadcast, then the CTA's arrival counter
   off += 32;
   L.bars = round_up(off, 8);  // full[slots], empty[slots]
@@ -766,6 +770,29 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
                 for (int mat = 0; mat < NW; ++mat) v[tok][mat] = red[(mat * MT + tok) * kRows + ptid];
             });
           finished(rb);
+        } else if (p.csize > 1) {
+          // Cluster split-K: this CTA's four ranges are its share of the row
+          // block's K.  The last pair to arrive adds the four pairs' shares (in
+          // pair order) and stores the CTA's sum into the cluster leader's
+          // shared memory; the leader adds the CTAs' sums in rank order after
+          // the cluster barrier at the end of the kernel.
+          int* flag = reinterpret_cast<int*>(sm + L.flag) + pair;
+          if (ptid == 0) *flag = (atom_add_acq_rel_cta_shared(base + L.flag + 16, 1u) == kPairs - 1);
+          named_barrier(bar, kPairThreads);
+          if (*flag && ptid < kRows) {
+            const uint32_t dst = mapa_shared(base + L.cred, 0) +
+                                 (uint32_t)(cluster_ctarank() * NW * MT * kRows + ptid) * 4u;
+#pragma unroll
+            for (int tok = 0; tok < MT; ++tok)
+#pragma unroll
+              for (int mat = 0; mat < NW; ++mat) {
+                float v = 0.f;
+#pragma unroll
+                for (int q = 0; q < kPairs; ++q)
+                  v += reinterpret_cast<const float*>(sm + L.red)[((q * NW + mat) * MT + tok) * kRows + ptid];
+                st_shared_cluster_f32(dst + (uint32_t)((mat * MT + tok) * kRows) * 4u, v);
+              }
+          }
         } else if (4 * (int)blockIdx.x + 3 < p.P && rb_lo == unit_begin(4 * blockIdx.x, p.U, p.P) &&
                    rb_hi == unit_begin(4 * blockIdx.x + 4, p.U, p.P)) {
           // This CTA's four ranges are exactly this row block (so each pair has
@@ -866,6 +893,27 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     }
   }
 
+  if (p.csize > 1) {
+    // every thread of every CTA of the cluster arrives here exactly once
+    cluster_sync_all();
+    if (cluster_ctarank() == 0 && warp < kCW) {
+      const int ptid = threadIdx.x;  // pair 0's threads
+      const int rb = (int)(unit_begin(kPairs * blockIdx.x, p.U, p.P) / p.TS);
+      if (ptid < kRows) {
+        finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](float(&v)[MT][NW]) {
+          const float* cred = reinterpret_cast<const float*>(sm + L.cred);
+#pragma unroll
+          for (int tok = 0; tok < MT; ++tok)
+#pragma unroll
+            for (int mat = 0; mat < NW; ++mat) {
+              v[tok][mat] = 0.f;
+              for (int r = 0; r < p.csize; ++r) v[tok][mat] += cred[((r * NW + mat) * MT + tok) * kRows + ptid];
+            }
+        });
+        if constexpr (is_tp(EPI)) tp_complete<MT, EPI>(p, rb, ptid, tp_e);
+      }
+    }
+  }
   if (!ok && p.status) atomicExch(p.status, kDevWaitTimeout);
 #ifdef FOCAL_TIMELINE
   __syncthreads();
@@ -988,6 +1036,22 @@ int ctas_per_sm(const void* kern, int slot, int smem, int dev, int* out) {
   return FOCAL_OK;
 }
 
+// Cluster split-K for small weight matrices: when C = 4 or 2 CTAs per row
+// block still fit in one wave and every one of a row block's 4C ranges gets a
+// unit, each row block's K is split over a cluster of C CTAs whose sums meet
+// in the leader's shared memory (no workspace round trip, which costs more
+// than a microsecond at the end of a small call).  FOCAL_W4A16_CLUSTER=1
+// turns it off (a tuning override).
+int split_k_plan(int RB, int TS, int sm_count) {
+  static const int allowed = [] {
+    const char* e = getenv("FOCAL_W4A16_CLUSTER");
+    return e ? atoi(e) : kMaxCluster;
+  }();
+  for (int c = kMaxCluster; c >= 2; c /= 2)
+    if (c <= allowed && RB * c <= sm_count && TS >= kPairs * c) return c;
+  return 1;
+}
+
 template <int MT, int NW, int EPI>
 int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
              uint8_t* workspace, size_t ws_bytes, const DeviceInfo& dev, cudaStream_t stream) {
@@ -1008,8 +1072,13 @@ int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
   // gets at least one unit (p.P <= U) so each row block's owners all report.
   (void)occ;  // the carve-up and register cap leave room for one CTA per SM
   static_assert(kPairs <= kMaxCtasPerSm, "workspace bound assumes at most kMaxCtasPerSm ranges per SM");
-  p.P = (int)std::min<long long>((p.U + min_units - 1) / min_units, (long long)kPairs * dev.sm_count);
-  p.P = std::max(p.P, 1);
+  p.csize = split_k_plan(p.RB, p.TS, dev.sm_count);
+  if (p.csize > 1) {
+    p.P = kPairs * p.csize * p.RB;  // CTA b: row block b / csize, K share b % csize
+  } else {
+    p.P = (int)std::min<long long>((p.U + min_units - 1) / min_units, (long long)kPairs * dev.sm_count);
+    p.P = std::max(p.P, 1);
+  }
   const int grid = (p.P + kPairs - 1) / kPairs;
   const WsLayout W = ws_layout(MT, NW, p.P);
   if (ws_bytes < W.total)
@@ -1022,9 +1091,16 @@ int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1] = {pdl_attribute()};
+  cudaLaunchAttribute attr[2] = {pdl_attribute(), {}};
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (p.csize > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)p.csize;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p),
                     "w4a16_gemv_kernel launch");
 }
