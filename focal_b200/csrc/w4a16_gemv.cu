@@ -1073,8 +1073,19 @@ int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
   (void)occ;  // the carve-up and register cap leave room for one CTA per SM
   static_assert(kPairs <= kMaxCtasPerSm, "workspace bound assumes at most kMaxCtasPerSm ranges per SM");
   p.csize = split_k_plan(p.RB, p.TS, dev.sm_count);
+  // Plans, in order of preference: cluster split-K (small matrices); one CTA
+  // per row block when the row blocks fit in one wave (its four ranges meet in
+  // shared memory, no workspace round trip); otherwise stream-K over all SMs
+  // with row blocks split across CTAs finished through the workspace.
+  // FOCAL_W4A16_ROWBLOCK=0 turns the second off (a tuning override).
+  static const bool rowblock = [] {
+    const char* e = getenv("FOCAL_W4A16_ROWBLOCK");
+    return !(e && atoi(e) == 0);
+  }();
   if (p.csize > 1) {
     p.P = kPairs * p.csize * p.RB;  // CTA b: row block b / csize, K share b % csize
+  } else if (rowblock && p.RB <= dev.sm_count && p.TS >= kPairs) {
+    p.P = kPairs * p.RB;  // CTA b: row block b
   } else {
     p.P = (int)std::min<long long>((p.U + min_units - 1) / min_units, (long long)kPairs * dev.sm_count);
     p.P = std::max(p.P, 1);
