@@ -41,6 +41,7 @@ SIGNATURES = {
     "focal_w4a16_workspace_size": (_S, [_I, _I, _I]),
     "focal_w4a16_gemv": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
     "focal_w4a16_gemv_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
+    "focal_w4a16_noalloc_scratch": (_I, [ctypes.POINTER(_P), ctypes.POINTER(_S)]),
     "focal_w4a16_gemv_f32": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
     "focal_w4a16_gate_up_silu": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _S, _P]),
     "focal_w4a16_tiles_size": (_S, [_I, _I]),
@@ -62,6 +63,7 @@ SIGNATURES = {
     "focal_gqa_decode_attn": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _S, _P]),
     "focal_gqa_decode_paged": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S, _P]),
     "focal_device_status": (_I, [ctypes.POINTER(_I)]),
+    "focal_device_status_peek": (_I, [ctypes.POINTER(_I)]),
     "focal_reset_device_status": (_I, []),
 }
 

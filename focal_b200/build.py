@@ -2,6 +2,7 @@
 
     python -m focal_b200.build          # both libraries
     python -m focal_b200.build --lib    # only the C-ABI library
+    python -m focal_b200.build --timeline  # also the per-unit timeline variant
 
 Outputs (next to this file, so they travel with the source tree):
 
@@ -31,6 +32,7 @@ ROOT = PKG.parent
 INCLUDE = ROOT / "include"
 BUILD = ROOT / "_build"
 LIB = PKG / "libfocal_b200.so"
+TIMELINE_LIB = PKG / "libfocal_b200_timeline.so"
 CU_SOURCES = ["capi.cu", "w4a16_gemv.cu", "w4a16_tiles.cu", "gqa_decode.cu"]
 HEADERS = ["common.cuh", "host_common.h", "w4a16_tiles.h"]
 
@@ -67,30 +69,37 @@ def _run(cmd, log: Path | None = None):
     return res
 
 
-def build_library(verbose: bool = False) -> Path:
-    BUILD.mkdir(exist_ok=True)
+def build_library(verbose: bool = False, timeline: bool = False) -> Path:
+    """The C-ABI library; with `timeline`, its diagnostic variant
+    libfocal_b200_timeline.so (-DFOCAL_TIMELINE: the GEMV kernel stamps SM
+    cycles per CTA, sub-pipeline, unit and phase into shared memory and copies
+    them to a buffer set with focal_tl_set), used only by bench.py --timeline."""
+    bdir = BUILD / "timeline" if timeline else BUILD
+    out = TIMELINE_LIB if timeline else LIB
+    bdir.mkdir(parents=True, exist_ok=True)
     nvcc = _nvcc()
     deps = [CSRC / h for h in HEADERS] + [INCLUDE / "focal_b200.h"]
+    extra = ["-DFOCAL_TIMELINE"] if timeline else []
     objs = []
     jobs = []
     for src in CU_SOURCES:
-        obj = BUILD / (Path(src).stem + ".o")
+        obj = bdir / (Path(src).stem + ".o")
         objs.append(obj)
         if not _newer(obj, [CSRC / src] + deps):
-            cmd = [nvcc, *NVCC_FLAGS, "-Xptxas", "-v", "-c", str(CSRC / src), "-o", str(obj)]
-            jobs.append((cmd, BUILD / (Path(src).stem + ".log")))
+            cmd = [nvcc, *NVCC_FLAGS, *extra, "-Xptxas", "-v", "-c", str(CSRC / src), "-o", str(obj)]
+            jobs.append((cmd, bdir / (Path(src).stem + ".log")))
     with cf.ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
         for f in [ex.submit(_run, c, l) for c, l in jobs]:
             f.result()
-    if not _newer(LIB, objs):
+    if not _newer(out, objs):
         _run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-cudart", "static",
-              "-Xlinker", "-soname,libfocal_b200.so", "-o", str(LIB), *map(str, objs)])
+              "-Xlinker", f"-soname,{out.name}", "-o", str(out), *map(str, objs)])
     if verbose:
         for src in CU_SOURCES:
-            log = BUILD / (Path(src).stem + ".log")
+            log = bdir / (Path(src).stem + ".log")
             if log.exists():
                 print(log.read_text())
-    return LIB
+    return out
 
 
 def torch_ext_path() -> Path:
@@ -134,9 +143,13 @@ def build_all(verbose: bool = False):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--lib", action="store_true", help="only the C-ABI library")
+    ap.add_argument("--timeline", action="store_true",
+                    help="also the per-unit timeline variant of the C-ABI library (bench.py --timeline)")
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args(argv)
     build_library(a.verbose)
+    if a.timeline:
+        build_library(a.verbose, timeline=True)
     if not a.lib:
         build_torch_ext(a.verbose)
     print("ok")

@@ -11,7 +11,6 @@
 namespace focal {
 
 // One status word per device; kernels whose bounded waits give up write it.
-__device__ int g_device_status;
 
 namespace {
 thread_local std::string g_last_error;
@@ -60,9 +59,17 @@ int current_device_info(DeviceInfo* out) {
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
     if (e == cudaSuccess && d.cc_major == 10) {
-      void* sp = nullptr;
-      e = cudaGetSymbolAddress(&sp, g_device_status);
-      d.status = static_cast<int*>(sp);
+      // the status word: one int of mapped pinned host memory per device, so
+      // the host reads it without synchronizing with the device
+      void* hp = nullptr;
+      e = cudaHostAlloc(&hp, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable);
+      if (e == cudaSuccess) {
+        *static_cast<volatile int*>(hp) = 0;
+        void* dp = nullptr;
+        e = cudaHostGetDevicePointer(&dp, hp, 0);
+        d.status = static_cast<int*>(dp);
+        d.status_host = static_cast<int*>(hp);
+      }
     }
     g_info_err[dev] = static_cast<int>(e);
     g_info[dev] = d;
@@ -116,11 +123,6 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, con
   return FOCAL_OK;
 }
 
-int* device_status_ptr() {
-  void* p = nullptr;
-  if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
-  return static_cast<int*>(p);
-}
 
 // ------------------------------------------------------------------ kernels
 // One thread per packed word: eight bytes in, one int32 out.
@@ -214,19 +216,32 @@ int focal_w4a16_dequant(const int32_t* wq, const void* scales, const void* zeros
 int focal_device_status(int* status_out) {
   clear_error();
   if (!status_out) return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
-  int v = 0;
-  int rc = check_cuda(cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)),
-                      "cudaMemcpyFromSymbol(status)");
+  DeviceInfo d;
+  int rc = current_device_info(&d);
   if (rc) return rc;
-  *status_out = v;
+  rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  if (rc) return rc;
+  *status_out = *static_cast<volatile int*>(d.status_host);
+  return FOCAL_OK;
+}
+
+int focal_device_status_peek(int* status_out) {
+  clear_error();
+  if (!status_out) return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
+  DeviceInfo d;
+  const int rc = current_device_info(&d);
+  if (rc) return rc;
+  *status_out = *static_cast<volatile int*>(d.status_host);
   return FOCAL_OK;
 }
 
 int focal_reset_device_status(void) {
   clear_error();
-  const int zero = 0;
-  return check_cuda(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)),
-                    "cudaMemcpyToSymbol(status)");
+  DeviceInfo d;
+  const int rc = current_device_info(&d);
+  if (rc) return rc;
+  *static_cast<volatile int*>(d.status_host) = 0;
+  return noalloc_clear_counters();
 }
 
 }  // extern "C"

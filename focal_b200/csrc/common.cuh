@@ -24,6 +24,14 @@ enum DeviceStatus : int {
 // ~2^31 SM cycles (about one second at 1.9 GHz) before a wait gives up.
 constexpr long long kWaitLimitCycles = 1LL << 31;
 
+// Record a device-side failure in the status word.  The word lives in mapped
+// pinned host memory (so the host can read it without a device sync), which is
+// why this is a plain system-scope store and not an atomic: any writer's
+// nonzero code is enough.
+__device__ __forceinline__ void set_status(int* status, int code) {
+  asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(status), "r"(code) : "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (PAGED) {
     L = p.seq_lens[b];
     if (L < 1 || L > p.L) {
-      if (threadIdx.x == 0 && split == 0) atomicExch(p.status, kDevBadIndex);
+      if (threadIdx.x == 0 && split == 0) set_status(p.status, kDevBadIndex);
       L = L < 1 ? 1 : p.L;
     }
   }
@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int q = first_page + 32 * c + lane;
         my_id = q <= last_page ? bt[q] : 0;
         if (my_id < 0 || my_id >= p.num_pages) {
-          atomicExch(p.status, kDevBadIndex);
+          set_status(p.status, kDevBadIndex);
           my_id = 0;
         }
       }
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     }
-    if (!ok && lane == 0 && p.status) atomicExch(p.status, kDevWaitTimeout);
+    if (!ok && lane == 0 && p.status) set_status(p.status, kDevWaitTimeout);
     return;
   }
   if (!PAGED && warp == kConsumerWarps) {
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         tma_load_3d(dst + 2 * kHalfBytes, &tmap_v, 0, pos, bh, fb, pol);
         tma_load_3d(dst + 3 * kHalfBytes, &tmap_v, 64, pos, bh, fb, pol);
       }
-      if (!ok && p.status) atomicExch(p.status, kDevWaitTimeout);
+      if (!ok && p.status) set_status(p.status, kDevWaitTimeout);
     }
     return;
   }
@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar + 8 * slot);
   }
-  if (!ok && p.status) atomicExch(p.status, kDevWaitTimeout);
+  if (!ok && p.status) set_status(p.status, kDevWaitTimeout);
 
   // ---- per-warp state -> shared memory (over the drained ring: wait for all warps)
 #pragma unroll

@@ -26,8 +26,12 @@ struct DeviceInfo {
   int sm_count = 0;
   int max_smem_optin = 0;  // bytes per block with opt-in
   int cc_major = 0, cc_minor = 0;
-  int* status = nullptr;  // device status word (see device_status_ptr)
+  int* status = nullptr;       // status word, device view (mapped pinned host memory)
+  int* status_host = nullptr;  // the same word, host view
 };
+
+// Zero the no-allocation GEMV scratch's counters on the current device (w4a16_gemv.cu).
+int noalloc_clear_counters();
 
 // Attributes of the current device (cached per device ordinal).
 int current_device_info(DeviceInfo* out);
@@ -42,7 +46,6 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, con
                       CUtensorMapSwizzle swizzle);
 
 // Per-device status word written by kernels whose bounded waits gave up.
-int* device_status_ptr();
 
 inline bool aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;

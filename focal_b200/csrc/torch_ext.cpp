@@ -46,8 +46,34 @@ std::mutex g_ws_mutex;
 std::map<std::tuple<int, int, cudaStream_t>, torch::Tensor> g_ws;
 std::vector<torch::Tensor> g_ws_retired;
 
+// A kernel that gave up a bounded device-side wait (a timed-out pipeline or
+// tensor-parallel peer) wrote a nonzero status word and may have left row-block
+// counters in a workspace nonzero.  Before every call that uses a workspace the
+// word is read (mapped host memory, no device sync); when it is set, every
+// cached workspace of the device is zeroed again on its own stream, the word is
+// cleared and the call raises, so the failure is reported once and later calls
+// are valid.  Called with g_ws_mutex held.
+void check_device_status_locked(const torch::Device& dev) {
+  int st = 0;
+  raise_on(focal_device_status_peek(&st));
+  if (st == 0) return;
+  for (auto& kv : g_ws)
+    if (std::get<1>(kv.first) == (int)dev.index()) {
+      const cudaError_t e =
+          cudaMemsetAsync(kv.second.data_ptr(), 0, (size_t)kv.second.numel(), std::get<2>(kv.first));
+      TORCH_CHECK(e == cudaSuccess, "cudaMemsetAsync (workspace reset): ", cudaGetErrorString(e));
+    }
+  raise_on(focal_reset_device_status());
+  TORCH_CHECK(false, "focal_b200: an earlier call on cuda:", (int)dev.index(),
+              " gave up a bounded device-side wait (status ", st,
+              st == 2 ? ": a tensor-parallel peer did not deliver" : st == 3 ? ": bad paged-KV index" : ": pipeline wait",
+              "); its output is invalid.  The cached workspaces were zeroed again and the status cleared; "
+              "later calls are valid.");
+}
+
 torch::Tensor workspace_for(WsKind kind, const torch::Device& dev, cudaStream_t stream, size_t bytes) {
   std::lock_guard<std::mutex> lock(g_ws_mutex);
+  check_device_status_locked(dev);
   auto key = std::make_tuple((int)kind, (int)dev.index(), stream);
   auto it = g_ws.find(key);
   if (it == g_ws.end() || (size_t)it->second.numel() < bytes) {

@@ -292,7 +292,8 @@ __device__ __forceinline__ void finish_block(const Params& p, int rb, int ptid, 
 // at the end of its range, so the exchange's NVLink latency overlaps the
 // pair's remaining units.
 template <int MT, int EPI>
-__device__ __forceinline__ void tp_complete(const Params& p, int rb, int ptid, unsigned int e) {
+__device__ __forceinline__ void tp_complete(const Params& p, int rb, int ptid, unsigned int e,
+                                            volatile int* gave_up) {
   constexpr int S = MT >= 8 ? 2 : MT >= 4 ? 4 : 8;  // source ranks polled together
   const size_t col = (size_t)rb * kRows + ptid;
   const size_t slab = (size_t)p.M * p.N;
@@ -317,8 +318,11 @@ __device__ __forceinline__ void tp_complete(const Params& p, int rb, int ptid, u
 #pragma unroll
         for (int i = 0; i < MT; ++i) ready = ready && (unsigned int)(w[j][i] >> 32) == e;
       if (ready) break;
-      if (clock64() - t0 > kWaitLimitCycles) {
-        atomicExch(p.status, kDevPeerTimeout);  // this block's output is garbage
+      // once any poll of this CTA has given up, later ones stop at once
+      // instead of each waiting out its own limit
+      if (*gave_up || clock64() - t0 > kWaitLimitCycles) {
+        *gave_up = 1;
+        set_status(p.status, kDevPeerTimeout);  // this block's output is garbage
         break;
       }
 #pragma unroll
@@ -354,6 +358,17 @@ __device__ __forceinline__ void tp_complete(const Params& p, int rb, int ptid, u
 }
 
 #ifdef FOCAL_TIMELINE
+// Diagnostic build only (libfocal_b200_timeline.so, read by bench.py
+// --timeline): per CTA (< kTlCtas), sub-pipeline and unit j (< kTlUnits) eight
+// stamps of SM cycles since the CTA's start, for the single-matrix kernels:
+//   0 producer issues the unit's weight boxes   1 producer's record arrival
+//   2 consumer (first warp of the pair) past the full-barrier wait
+//   3 consumer done with the unit                4 consumer at the top of its loop
+//   5 consumer's shared-memory loads issued       6 consumer's MMA block done
+//   7 second consumer warp done
+// Unit slot 63 holds the pair's run end instead (0 start, 3 done).  Per CTA,
+// eight 64-bit words follow the stamps: start clock, start %globaltimer, end
+// clock, end %globaltimer, and the producer's clock after griddepcontrol.wait.
 constexpr int kTlCtas = 160, kTlUnits = 64;
 __device__ long long* g_tl;
 __device__ __forceinline__ long long gtimer() {
@@ -365,7 +380,7 @@ __device__ __forceinline__ long long gtimer() {
 // copied out at the end, so they add no global stores to the timed loop
 #define TL(ev, j)                                                                                        \
   do {                                                                                                   \
-    if (NW == 1 && (j) < kTlUnits)                                                                               \
+    if (NW == 1 && (j) < kTlUnits)                                                                       \
       reinterpret_cast<volatile uint32_t*>(sm + L.tl)[(pair * kTlUnits + (j)) * 8 + (ev)] =              \
           (uint32_t)(clock64() - tl_t0);                                                                 \
   } while (0)
@@ -414,6 +429,7 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
   if (NW == 1)
     for (int i = threadIdx.x; i < kPairs * kTlUnits * 8; i += blockDim.x) reinterpret_cast<uint32_t*>(sm + L.tl)[i] = 0u;
 #endif
+  volatile int* tp_gave_up = reinterpret_cast<volatile int*>(sm + L.flag + 20);
   const uint32_t full_bar = base + L.bars;
   const uint32_t empty_bar = full_bar + kSlots * 8;
 
@@ -426,6 +442,7 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
       mbar_init(empty_bar + 8 * s, kCW);  // the sub-pipeline's consumer warps
     }
     *reinterpret_cast<unsigned int*>(sm + L.flag + 16) = 0u;  // in-CTA row-block arrivals
+    *reinterpret_cast<int*>(sm + L.flag + 20) = 0;            // a tensor-parallel poll gave up
     fence_barrier_init();
     griddep_launch_dependents();
   }
@@ -619,7 +636,7 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     int pend_rb = -1;  // tensor-parallel: a row block this pair sent but has not completed
     auto finished = [&](int frb) {
       if constexpr (is_tp(EPI)) {
-        if (pend_rb >= 0 && ptid < kRows) tp_complete<MT, EPI>(p, pend_rb, ptid, tp_e);
+        if (pend_rb >= 0 && ptid < kRows) tp_complete<MT, EPI>(p, pend_rb, ptid, tp_e, tp_gave_up);
         pend_rb = frb;
       }
     };
@@ -889,7 +906,7 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
       }
     }
     if constexpr (is_tp(EPI)) {
-      if (pend_rb >= 0 && ptid < kRows) tp_complete<MT, EPI>(p, pend_rb, ptid, tp_e);
+      if (pend_rb >= 0 && ptid < kRows) tp_complete<MT, EPI>(p, pend_rb, ptid, tp_e, tp_gave_up);
     }
   }
 
@@ -910,11 +927,11 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
               for (int r = 0; r < p.csize; ++r) v[tok][mat] += cred[((r * NW + mat) * MT + tok) * kRows + ptid];
             }
         });
-        if constexpr (is_tp(EPI)) tp_complete<MT, EPI>(p, rb, ptid, tp_e);
+        if constexpr (is_tp(EPI)) tp_complete<MT, EPI>(p, rb, ptid, tp_e, tp_gave_up);
       }
     }
   }
-  if (!ok && p.status) atomicExch(p.status, kDevWaitTimeout);
+  if (!ok && p.status) set_status(p.status, kDevWaitTimeout);
 #ifdef FOCAL_TIMELINE
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -1305,6 +1322,40 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 std::mutex g_noalloc_mutex;
 void* g_noalloc_ptr[64] = {};
 
+// The scratch's device address on the current device, resolved once per device.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return set_error(FOCAL_ERR_INVALID_VALUE, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    rc = check_cuda(cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_noalloc_scratch), "cudaGetSymbolAddress");
+    if (rc) return rc;
+  }
+  *out = g_noalloc_ptr[dev];
+  return FOCAL_OK;
+}
+
+}  // namespace gemv
+
+// Zero the no-allocation scratch's row-block counters on the current device if
+// they have been used there (after a device-side wait gave up they may be left
+// nonzero).  Allocates nothing.
+int noalloc_clear_counters() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FOCAL_OK;
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(gemv::g_noalloc_mutex);
+    ptr = gemv::g_noalloc_ptr[dev];
+  }
+  if (!ptr) return FOCAL_OK;
+  return check_cuda(cudaMemset(ptr, 0, gemv::kCounterBytes), "cudaMemset(no-allocation scratch counters)");
+}
+
+namespace gemv {
+
 }  // namespace gemv
 }  // namespace focal
 
@@ -1431,6 +1482,7 @@ int focal_w4a16_gate_up_silu_tiled(const void* x, const void* tiles_gate, const 
 }
 
 #ifdef FOCAL_TIMELINE
+// Diagnostic build only: where the GEMV kernel copies its stamps (null: off).
 int focal_tl_set(void* buf) {
   return cudaMemcpyToSymbol(gemv::g_tl, &buf, sizeof(buf)) == cudaSuccess ? 0 : 4;
 }
@@ -1442,27 +1494,30 @@ int focal_w4a16_gemv_noalloc(const void* x, const int32_t* wq, const void* scale
   int rc = gemv::check_shape(M, K, N);
   if (rc) return rc;
   const size_t need = focal_w4a16_workspace_size(M, K, N);
-  if (need > gemv::kNoAllocScratchBytes)
+  // FOCAL_W4A16_NOALLOC_LIMIT lowers the limit (a test hook for the error path,
+  // which no shape reaches on a 148-SM B200)
+  const char* lim_env = getenv("FOCAL_W4A16_NOALLOC_LIMIT");
+  const size_t limit = lim_env && atoll(lim_env) > 0 ? std::min<size_t>((size_t)atoll(lim_env), gemv::kNoAllocScratchBytes)
+                                                   : gemv::kNoAllocScratchBytes;
+  if (need > limit)
     return set_error(FOCAL_ERR_UNSUPPORTED,
                      "focal_w4a16_gemv_noalloc: M=%d K=%d N=%d needs %zu bytes of scratch, more than its "
                      "fixed %zu; call focal_w4a16_gemv with a workspace instead",
-                     M, K, N, need, gemv::kNoAllocScratchBytes);
-  int dev = 0;
-  rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-  if (rc) return rc;
-  if (dev < 0 || dev >= 64) return set_error(FOCAL_ERR_INVALID_VALUE, "device %d out of range", dev);
+                     M, K, N, need, limit);
   void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(gemv::g_noalloc_mutex);
-    if (!gemv::g_noalloc_ptr[dev]) {
-      rc = check_cuda(cudaGetSymbolAddress(&gemv::g_noalloc_ptr[dev], gemv::g_noalloc_scratch),
-                      "cudaGetSymbolAddress");
-      if (rc) return rc;
-    }
-    scratch = gemv::g_noalloc_ptr[dev];
-  }
+  rc = gemv::noalloc_scratch(&scratch);
+  if (rc) return rc;
   return gemv::run(gemv::kEpiBf16, x, wq, scales, zeros, nullptr, nullptr, nullptr, y, M, K, N, scratch,
                    gemv::kNoAllocScratchBytes, stream);
+}
+
+int focal_w4a16_noalloc_scratch(void** scratch, size_t* bytes) {
+  clear_error();
+  if (!scratch || !bytes) return set_error(FOCAL_ERR_INVALID_VALUE, "null pointer");
+  const int rc = gemv::noalloc_scratch(scratch);
+  if (rc) return rc;
+  *bytes = gemv::kNoAllocScratchBytes;
+  return FOCAL_OK;
 }
 
 }  // extern "C"

@@ -84,13 +84,18 @@ int focal_w4a16_gemv(const void* x, const int32_t* wq, const void* scales, const
  *    (cudaGetSymbolAddress); make it before any stream capture.
  *  - The scratch's arrival counters start at zero when the library loads and
  *    every successful call leaves them at zero; after a call that failed on the
- *    device (focal_device_status nonzero) the results of later calls are not
- *    defined until the process restarts.
+ *    device (focal_device_status nonzero) they may not be:
+ *    focal_reset_device_status zeroes them again (a memset, no allocation).
  *  - All calls on one device share the scratch, so calls that may overlap
  *    (different streams, or host threads without ordering) race; order them on
  *    one stream. */
 int focal_w4a16_gemv_noalloc(const void* x, const int32_t* wq, const void* scales, const void* zeros,
                              void* y, int M, int K, int N, cudaStream_t stream);
+
+/* Diagnostic: the no-allocation scratch of the current device (its device
+ * address, resolved on first use, and its size in bytes).  No reference
+ * counterpart. */
+int focal_w4a16_noalloc_scratch(void** scratch, size_t* bytes);
 
 /* Same product with an fp32 output (no bf16 rounding): the partial sum of a
  * K-sharded (row-parallel) projection before its all-reduce.  New entry point;
@@ -252,8 +257,15 @@ int focal_gqa_decode_paged(const void* q, const void* k_pages, const void* v_pag
  * bounded waits have completed; otherwise 1 (a pipeline wait gave up), 2 (a
  * tensor-parallel peer did not deliver in time) or 3 (a paged-KV page id or
  * sequence length out of range).
- * Synchronous (reads device memory).  focal_reset_device_status clears it. */
+ * The word lives in mapped pinned host memory, one per device.
+ * focal_device_status synchronizes the device first, so it covers every call
+ * made before it; focal_device_status_peek reads the word as it stands (calls
+ * that have finished), with no synchronization, so a caller can check it
+ * before each launch (the PyTorch wrapper does, and on a nonzero word re-zeroes
+ * its cached workspaces and raises).  focal_reset_device_status clears it.
+ * (No counterpart in the reference, which has no bounded device waits.) */
 int focal_device_status(int* status_out);
+int focal_device_status_peek(int* status_out);
 int focal_reset_device_status(void);
 
 #ifdef __cplusplus

@@ -123,3 +123,39 @@ def test_missing_peer_times_out_with_status(cuda):
                                       2e-2, 1e-2)
     assert assert_close["allclose"], assert_close
     assert L.focal_device_status(status) == 0 and status.value == 0
+
+
+def test_device_failure_is_reported_to_torch_callers(cuda):
+    """After a kernel gives up a bounded wait (a two-rank group whose peer never
+    writes, as above), the next PyTorch-level call raises instead of returning
+    numbers computed on possibly stale counters; it clears the status and
+    re-zeroes the cached workspaces, and the call after it matches the oracle."""
+    import ctypes
+
+    import focal_w4a16
+    from focal_b200 import _lib
+
+    L = _lib.lib()
+    M, K, N = 1, 1024, 256
+    nbytes = int(L.focal_tp_buffer_size(2, M, N))
+    bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=cuda) for _ in range(2)]
+    comm = _lib.TpComm()
+    comm.peer[0], comm.peer[1] = bufs[0].data_ptr(), bufs[1].data_ptr()
+    comm.bytes, comm.world, comm.rank = nbytes, 2, 0
+    case = ow.baseline_case(M, K, N, seed=6)
+    x, wq, s, z = (C.to_dev_bf16(a, cuda) if j == 0 else C.to_dev(a, cuda) for j, a in enumerate(case))
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
+    ws, n = C.w4a16_workspace(M, K, N, cuda)
+    assert L.focal_reset_device_status() == 0
+    focal_w4a16.w4a16_linear(x, wq, s, z)  # the cached workspace exists before the failure
+    assert L.focal_w4a16_gemv_allreduce(x.data_ptr(), wq.data_ptr(), s.data_ptr(), z.data_ptr(), y.data_ptr(),
+                                        M, K, N, ctypes.byref(comm), ws.data_ptr(), n, C.stream_ptr()) == 0
+    torch.cuda.synchronize()
+    peek = ctypes.c_int(-1)
+    assert L.focal_device_status_peek(peek) == 0 and peek.value == 2
+    with pytest.raises(RuntimeError, match="gave up a bounded device-side wait"):
+        focal_w4a16.w4a16_linear(x, wq, s, z)
+    assert L.focal_device_status_peek(peek) == 0 and peek.value == 0
+    got = focal_w4a16.w4a16_linear(x, wq, s, z)
+    rep = ow.allclose_report(C.bf16_bits(got), ow.linear(*case), 2e-2, 1e-2)
+    assert rep["allclose"], rep

@@ -190,3 +190,24 @@ def test_capi_rejects_bad_shapes_and_pointers(cuda):
     assert rc == _lib.FOCAL_ERR_WORKSPACE
     status = __import__("ctypes").c_int(-1)
     assert L.focal_device_status(status) == 0 and status.value == 0
+
+
+@pytest.mark.parametrize("M", [1, 8])
+def test_decode_mlp_end_to_end(cuda, M):
+    """focal_b200.decode_mlp (fused gate/up with SiLU*up, then the down
+    projection) at the Llama-2-7B MLP shape against the oracle's composition of
+    the same three linears."""
+    import focal_b200 as F
+
+    H, I = 4096, 11008
+    x, wg, sg, zg = ow.baseline_case(M, H, I, seed=1200 + M)
+    _, wu, su, zu = ow.baseline_case(1, H, I, seed=1250 + M)
+    _, wd, sd, zd = ow.baseline_case(1, I, H, seed=1300 + M)
+    h_ref = silu_mul_oracle(ow.linear(x, wg, sg, zg), ow.linear(x, wu, su, zu))
+    ref = ow.linear(h_ref, wd, sd, zd)
+    dev = lambda *a: tuple(C.to_dev(v, cuda) for v in a)  # noqa: E731
+    y = F.decode_mlp(C.to_dev_bf16(x, cuda), dev(wg, sg, zg), dev(wu, su, zu), dev(wd, sd, zd))
+    assert y.shape == (M, H) and y.dtype == torch.bfloat16
+    # the hidden activations can differ from the oracle's by one bf16 step,
+    # which the down projection carries into y: bound the relative error
+    assert_parity(y, ref, f"M={M}", reference_metric=False)

@@ -44,3 +44,40 @@ def test_noalloc_matches_workspace_entry_point(cuda, M, K, N):
         outs.append(y_na)
     # the second call did not disturb the first call's result
     assert not torch.equal(outs[0], outs[1])
+
+
+class _DevBytes:
+    """A zero-copy uint8 view of device memory at `ptr` (for reading the scratch)."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, True), "version": 3}
+
+
+def test_noalloc_leaves_counters_zero(cuda):
+    """Every call leaves the scratch's row-block arrival counters (its first
+    16 KiB) at zero, including shapes whose row blocks are split across CTAs
+    and finished through those counters (K=8192, N=11008)."""
+    import ctypes
+
+    for (M, K, N) in [(8, 8192, 11008), (1, 4096, 4096)]:
+        x, wq, s, z = ow.baseline_case(M, K, N, seed=77)
+        noalloc(C.to_dev_bf16(x, cuda), C.to_dev(wq, cuda), C.to_dev(s, cuda), C.to_dev(z, cuda))
+    torch.cuda.synchronize()
+    ptr, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
+    _lib.call("focal_w4a16_noalloc_scratch", ctypes.byref(ptr), ctypes.byref(nbytes))
+    assert nbytes.value == 8 << 20
+    counters = torch.as_tensor(_DevBytes(ptr.value, 16 << 10), device=cuda)
+    assert int(counters.count_nonzero()) == 0
+
+
+def test_noalloc_rejects_shapes_beyond_its_scratch(cuda, monkeypatch):
+    """A shape whose workspace bound exceeds the scratch is refused with
+    FOCAL_ERR_UNSUPPORTED and a message that names the limit.  No contract shape
+    reaches the 8 MiB on a 148-SM B200, so the limit is lowered through the
+    library's test hook."""
+    monkeypatch.setenv("FOCAL_W4A16_NOALLOC_LIMIT", "4096")
+    x, wq, s, z = ow.baseline_case(1, 4096, 4096, seed=78)
+    with pytest.raises(_lib.FocalError) as e:
+        noalloc(C.to_dev_bf16(x, cuda), C.to_dev(wq, cuda), C.to_dev(s, cuda), C.to_dev(z, cuda))
+    assert e.value.code == _lib.FOCAL_ERR_UNSUPPORTED
+    assert "scratch" in str(e.value) and "4096" in str(e.value)
