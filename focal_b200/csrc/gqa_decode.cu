@@ -31,6 +31,7 @@
 // length needs; block-table entries or lengths out of range set the device
 // status (kDevBadIndex) and are clamped.
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "host_common.h"
@@ -42,12 +43,14 @@ constexpr int kD = 128;
 constexpr int kTile = 64;              // positions per stage
 constexpr int kConsumerWarps = 4;      // 16 positions each
 constexpr int kThreads = 32 * (kConsumerWarps + 1);
-constexpr int kStages = 3;
+constexpr int kStages = 3;       // ring stages at two CTAs per SM
+constexpr int kStagesDeep = 6;   // ring stages when a plan gives each SM one CTA
 constexpr int kHalfBytes = kTile * 128;        // 64 positions x 64 dims x 2 B
 constexpr int kKVStageBytes = 4 * kHalfBytes;  // K lo/hi + V lo/hi
 constexpr int kMaxGroup = 16;
 constexpr int kMaxSplits = 128;
 constexpr int kCounterBytes = 256;     // counters region granularity
+constexpr int kCombineBatch = 8;      // split partials loaded together by the combining CTA
 
 struct Params {
   const int32_t* block_table;  // paged: [B, max_pages]
@@ -68,7 +71,7 @@ struct Params {
 constexpr int kRingBytes = kStages * kKVStageBytes;
 constexpr int kWarpOBytes = kConsumerWarps * kMaxGroup * kD * 4;
 constexpr int kWarpMLBytes = kConsumerWarps * kMaxGroup * 2 * 4;
-constexpr int kSmemBytes = 1024 + kRingBytes + kWarpMLBytes + 16 + 2 * kStages * 8;
+__host__ __device__ constexpr int smem_bytes(int st) { return 1024 + st * kKVStageBytes + kWarpMLBytes + 16 + 2 * st * 8; }
 static_assert(kWarpOBytes <= kRingBytes, "warp partials alias the K/V ring");
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -82,10 +85,12 @@ __device__ __forceinline__ uint32_t tile_off(int p, int c) {
   return (c >> 3) * kHalfBytes + p * 128 + (((c & 7) ^ (p & 7)) << 4);
 }
 
-template <bool PAGED>
-__global__ void __launch_bounds__(kThreads, 2)
+template <bool PAGED, int ST>
+__global__ void __launch_bounds__(kThreads, 1)
     gqa_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v, const Params p) {
+  constexpr int kStages = ST;  // ring depth of this instantiation
+  constexpr int kRingBytes = ST * kKVStageBytes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -408,21 +413,45 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int row = e / (kD / 4);
     const int d = (e - row * (kD / 4)) * 4;
     const size_t rec0 = (size_t)bh * p.splits * grp + row;
-    float mm = -INFINITY;
-    for (int s = 0; s < splits; ++s) mm = fmaxf(mm, __ldcg(p.part_ml + (rec0 + (size_t)s * grp) * 2));
-    const float mu = mm == -INFINITY ? 0.f : mm;
+    // One pass in split order, kCombineBatch splits' partials loaded together
+    // (one L2 round trip per batch), merged online: the running sums are
+    // rescaled when a batch raises the running maximum.
+    float mu = -INFINITY;  // running maximum (log2 domain)
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float l = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      const size_t rec = rec0 + (size_t)s * grp;
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + rec * 2));
-      const float wgt = fast_exp2(ml.x - mu);
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(p.part_o + rec * kD + d));
-      acc.x += wgt * v.x;
-      acc.y += wgt * v.y;
-      acc.z += wgt * v.z;
-      acc.w += wgt * v.w;
-      l += wgt * ml.y;
+    for (int s0 = 0; s0 < splits; s0 += kCombineBatch) {
+      float2 ml[kCombineBatch];
+      float4 v[kCombineBatch];
+#pragma unroll
+      for (int u = 0; u < kCombineBatch; ++u) {
+        ml[u] = make_float2(-INFINITY, 0.f);
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s0 + u < splits) {
+          const size_t rec = rec0 + (size_t)(s0 + u) * grp;
+          ml[u] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + rec * 2));
+          v[u] = __ldcg(reinterpret_cast<const float4*>(p.part_o + rec * kD + d));
+        }
+      }
+      float nm = mu;
+#pragma unroll
+      for (int u = 0; u < kCombineBatch; ++u) nm = fmaxf(nm, ml[u].x);
+      if (nm == -INFINITY) continue;  // nothing but empty splits so far
+      const float r = fast_exp2(mu - nm);  // 0 while mu is still -inf
+      acc.x *= r;
+      acc.y *= r;
+      acc.z *= r;
+      acc.w *= r;
+      l *= r;
+#pragma unroll
+      for (int u = 0; u < kCombineBatch; ++u) {
+        const float wgt = fast_exp2(ml[u].x - nm);
+        acc.x += wgt * v[u].x;
+        acc.y += wgt * v[u].y;
+        acc.z += wgt * v[u].z;
+        acc.w += wgt * v[u].w;
+        l += wgt * ml[u].y;
+      }
+      mu = nm;
     }
     const float inv = 1.0f / l;
     __nv_bfloat16* dst = p.o + ((size_t)b * p.Hq + (size_t)kvh * grp + row) * kD + d;
@@ -443,10 +472,27 @@ Plan make_plan(int B, int Hkv, int L, int sm_count) {
   const int bhn = B * Hkv;
   // Two CTAs per SM fit in shared memory; stay within one resident wave so
   // every CTA streams the same number of tiles at the same time.
-  const int target = 2 * sm_count;
+  // Long sequences: one CTA per SM (launched with the 6-stage ring), each
+  // split streaming at least four tiles; short ones: two CTAs per SM, so more
+  // splits start at once.  FOCAL_ATTN_CTAS_PER_SM forces either (tuning).
+  static const int per_sm_env = [] {
+    const char* e = getenv("FOCAL_ATTN_CTAS_PER_SM");
+    return e && atoi(e) > 0 ? atoi(e) : 0;
+  }();
+  static const int min_tiles = [] {  // tuning override
+    const char* e = getenv("FOCAL_ATTN_MIN_TILES");
+    return e && atoi(e) > 0 ? atoi(e) : 1;
+  }();
+  int per_sm = per_sm_env;
+  if (per_sm == 0) {
+    const int s1 = sm_count / bhn;
+    per_sm = (s1 >= 1 && pl.tiles / s1 >= 4) ? 1 : 2;
+  }
+  const int target = per_sm * sm_count;
   int s = target / bhn;
   s = s < 1 ? 1 : s;
   s = s > pl.tiles ? pl.tiles : s;
+  if (min_tiles > 1 && s > 1 && pl.tiles / s < min_tiles) s = pl.tiles / min_tiles > 1 ? pl.tiles / min_tiles : 1;
   s = s > kMaxSplits ? kMaxSplits : s;
   pl.tiles_per_split = (pl.tiles + s - 1) / s;
   pl.splits = (pl.tiles + pl.tiles_per_split - 1) / pl.tiles_per_split;
@@ -505,10 +551,13 @@ int fill_params(Params* pp, const void* q, void* o, int B, int Hq, int Hkv, int 
   return FOCAL_OK;
 }
 
-template <bool PAGED>
-int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, int bhn, cudaStream_t stream) {
-  auto kern = gqa_decode_kernel<PAGED>;
-  int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), PAGED ? 41 : 40, kSmemBytes);
+template <bool PAGED, int ST>
+int launch_st(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, int bhn, cudaStream_t stream) {
+  auto kern = gqa_decode_kernel<PAGED, ST>;
+  constexpr int kSmemBytes = smem_bytes(ST);
+  static_assert(smem_bytes(ST) <= 227 * 1024, "shared memory per CTA");
+  int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (PAGED ? 41 : 40) + (ST == kStages ? 0 : 2),
+                               kSmemBytes);
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.splits, bhn, 1);
@@ -521,6 +570,15 @@ int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, int bh
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, mk, mv, p), "gqa_decode_kernel launch");
+}
+
+// Two CTAs per SM use the 3-stage ring; a plan whose grid fits one CTA per SM
+// gets the 6-stage ring (twice the bytes in flight per SM).
+template <bool PAGED>
+int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, int bhn, cudaStream_t stream,
+           int sm_count) {
+  if (p.splits * bhn <= sm_count) return launch_st<PAGED, kStagesDeep>(mk, mv, p, bhn, stream);
+  return launch_st<PAGED, kStages>(mk, mv, p, bhn, stream);
 }
 
 }  // namespace attn
@@ -566,7 +624,7 @@ int focal_gqa_decode_attn(const void* q, const void* k, const void* v, void* o, 
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
 
-  return attn::launch<false>(mk, mv, p, bhn, stream);
+  return attn::launch<false>(mk, mv, p, bhn, stream, dev.sm_count);
 }
 
 int focal_gqa_decode_paged(const void* q, const void* k_pages, const void* v_pages, const int32_t* block_table,
@@ -615,7 +673,7 @@ int focal_gqa_decode_paged(const void* q, const void* k_pages, const void* v_pag
   rc = encode_tensor_map(&mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v_pages, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  return attn::launch<true>(mk, mv, p, bhn, stream);
+  return attn::launch<true>(mk, mv, p, bhn, stream, dev.sm_count);
 }
 
 }  // extern "C"

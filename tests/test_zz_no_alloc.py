@@ -50,7 +50,7 @@ class _DevBytes:
     """A zero-copy uint8 view of device memory at `ptr` (for reading the scratch)."""
 
     def __init__(self, ptr, n):
-        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, True), "version": 3}
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False), "version": 3}
 
 
 def test_noalloc_leaves_counters_zero(cuda):
