@@ -358,8 +358,22 @@ def per_shape_graph(device, peak, repeats=7):
         cases = weight_copies(F.baseline_case(M, K, N, seed=3000 + i, device=device), copies, device, 77 + i)
         cold, _ = graph_time_us([(lambda c=c: F.w4a16_linear(*c)) for c in cases], device, repeats)
         warm, _ = graph_time_us([lambda: F.w4a16_linear(*cases[0])] * 16, device, repeats)
+        # the reference's own timing (bench/bench_w4a16.py time_cuda): eager
+        # calls on one weight set, back to back between two events, mean per call
+        for _ in range(10):
+            F.w4a16_linear(*cases[0])
+        torch.cuda.synchronize(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(100):
+            F.w4a16_linear(*cases[0])
+        e1.record()
+        torch.cuda.synchronize(device)
+        refstyle = e0.elapsed_time(e1) * 1e3 / 100
         rows.append({"M": M, "K": K, "N": N, "us": round(cold, 3), "GBps": round(nb / cold / 1e3, 1),
-                     "frac": round(nb / cold / 1e3 / peak, 3), "us_warm": round(warm, 3)})
+                     "frac": round(nb / cold / 1e3 / peak, 3), "us_warm": round(warm, 3),
+                     "us_refstyle": round(refstyle, 3)})
         del cases
     torch.cuda.empty_cache()
     return rows
@@ -637,8 +651,9 @@ def run_ours(args, rank, world, local):
             "device_status": status.value,
             "per_shape": per_shape,
             "per_shape_note": "us: CUDA graph of L2-cold calls (rotating weight copies), median of 7; "
-                              "us_warm: same weights back to back in a graph; us_eager: one eager call "
-                              "between two events (includes launch processing)",
+                              "us_warm: same weights back to back in a graph; us_refstyle: 100 eager calls on "
+                              "one weight set back to back, mean (the reference benchmark's method); us_eager: "
+                              "one eager call between two events (includes launch processing)",
             **extra,
         }
         if tp is not None:
