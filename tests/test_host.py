@@ -117,3 +117,12 @@ def test_paged_attention_argument_errors_without_gpu():
     assert call(page_size=16, max_pages=4) == _lib.FOCAL_ERR_UNSUPPORTED and "max_seq_len" in _lib.last_error()
     assert call(page_size=64, D=64) == _lib.FOCAL_ERR_UNSUPPORTED and "head_dim" in _lib.last_error()
     assert call(page_size=128) == _lib.FOCAL_ERR_INVALID_VALUE and "null" in _lib.last_error()
+
+def test_reference_extension_module_name_resolves():
+    """`import focal_w4a16._C` (the module the reference package imports) loads
+    the B200 extension and exposes its entry points; no GPU is touched."""
+    import importlib
+
+    m = importlib.import_module("focal_w4a16._C")
+    for name in ("w4a16_linear", "w4a16_linear_f32", "w4a16_gate_up_silu", "gqa_decode_attention"):
+        assert callable(getattr(m, name)), name
