@@ -613,7 +613,6 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     // permutation keeps the swizzled reads conflict-free, and because every such
     // row is pg mod 8 the 128-byte swizzle maps chunk 4G+t to one column for all.
     const int pg = (g >> 1) + ((g & 1) << 2);
-    const bool has_token = g < p.M;
     const int gc = g < MT ? g : 0;
     const uint32_t kMask = 0x000F000Fu, kMagic = 0x43004300u;  // held in registers
     const uint32_t w_lane = L.w + pg * 128 + ((uint32_t)((4 * G + t) ^ pg) << 4);
@@ -624,7 +623,6 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     const uint32_t rs = p.sz_tma ? 16u : 4u;
     const uint32_t sz_mat = 2 * kRows * rs;  // bytes per (slot, mat)
     const uint32_t sz_lane = L.sz + pg * rs;
-    const int half_shift = 16 * G;  // this group's fp16 within a scale/zero pair
     float acc[NW][kTPW][4];
 #pragma unroll
     for (int mat = 0; mat < NW; ++mat)
@@ -664,8 +662,9 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
         uint32_t xb[16];
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
-          uint4 v = make_uint4(0u, 0u, 0u, 0u);
-          if (has_token) v = lds128(base + x_off[qq] + xso);
+          // lanes of tokens >= M read token 0's fragments (x_off uses gc); their
+          // MMA columns are never stored
+          const uint4 v = lds128(base + x_off[qq] + xso);
           xb[4 * qq + 0] = v.x;
           xb[4 * qq + 1] = v.y;
           xb[4 * qq + 2] = v.z;
@@ -697,8 +696,8 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
             for (int hf = 0; hf < 2; ++hf) {
               const uint32_t r = 16 * tl + 8 * hf;  // rows beyond pg
               wv[tl][hf] = lds128(base + wb + r * 128);
-              sv[tl][hf] = lds32(base + sb + r * rs) >> half_shift;
-              zv[tl][hf] = lds32(base + sb + (kRows + r) * rs) >> half_shift;
+              sv[tl][hf] = lds_u16(base + sb + r * rs + 2 * G);
+              zv[tl][hf] = lds_u16(base + sb + (kRows + r) * rs + 2 * G);
             }
           }
           float d[kTPW][4];
