@@ -473,8 +473,8 @@ Plan make_plan(int B, int Hkv, int L, int sm_count) {
   // Two CTAs per SM fit in shared memory; stay within one resident wave so
   // every CTA streams the same number of tiles at the same time.
   // Long sequences: one CTA per SM (launched with the 6-stage ring), each
-  // split streaming at least four tiles; short ones: two CTAs per SM, so more
-  // splits start at once.  FOCAL_ATTN_CTAS_PER_SM forces either (tuning).
+  // split streaming at least four tiles, when that still covers 90 % of the
+  // SMs; otherwise two CTAs per SM, so more splits start at once.  FOCAL_ATTN_CTAS_PER_SM forces either (tuning).
   static const int per_sm_env = [] {
     const char* e = getenv("FOCAL_ATTN_CTAS_PER_SM");
     return e && atoi(e) > 0 ? atoi(e) : 0;
@@ -486,7 +486,7 @@ Plan make_plan(int B, int Hkv, int L, int sm_count) {
   int per_sm = per_sm_env;
   if (per_sm == 0) {
     const int s1 = sm_count / bhn;
-    per_sm = (s1 >= 1 && pl.tiles / s1 >= 4) ? 1 : 2;
+    per_sm = (s1 >= 1 && pl.tiles / s1 >= 4 && 10 * bhn * s1 >= 9 * sm_count) ? 1 : 2;
   }
   const int target = per_sm * sm_count;
   int s = target / bhn;

@@ -393,7 +393,10 @@ __device__ __forceinline__ long long gtimer() {
 #define TLH(i, v)
 #endif
 
-template <int MT, int NW, int EPI>
+// SZQ: scales / zeros arrive as TMA quads (16-byte staging rows) rather than as
+// the unit's two groups per row (4-byte rows); a template parameter so the
+// consumers' staging addresses are a base register plus immediate offsets.
+template <int MT, int NW, int EPI, bool SZQ>
 __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     w4a16_gemv_kernel(const __grid_constant__ CUtensorMap tmap0, const __grid_constant__ CUtensorMap tmap1,
                       const __grid_constant__ CUtensorMap tms0, const __grid_constant__ CUtensorMap tmz0,
@@ -438,7 +441,7 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     for (int s = 0; s < kSlots; ++s) {
       // the producer's expect_tx and its activation-record arrival, plus 32
       // cp.async arrivals when scales / zeros use cp.async
-      mbar_init(full_bar + 8 * s, (p.sz_tma || p.tiles0) ? 2 : 2 + 32);
+      mbar_init(full_bar + 8 * s, (SZQ || p.tiles0) ? 2 : 2 + 32);
       mbar_init(empty_bar + 8 * s, kCW);  // the sub-pipeline's consumer warps
     }
     *reinterpret_cast<unsigned int*>(sm + L.flag + 16) = 0u;  // in-CTA row-block arrivals
@@ -458,7 +461,7 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     if (lane == 0 && !p.tiles0) {
       prefetch_tensormap(&tmap0);
       if (NW == 2) prefetch_tensormap(&tmap1);
-      if (p.sz_tma) {
+      if (SZQ) {
         prefetch_tensormap(&tms0);
         prefetch_tensormap(&tmz0);
         if (NW == 2) {
@@ -489,7 +492,7 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
         }
         return;
       }
-      const bool szq = p.sz_tma && opens_quad;
+      const bool szq = SZQ && opens_quad;
       mbar_arrive_expect_tx(fb, NW * kRows * 128 + (szq ? NW * 2 * kRows * 16 : 0));
       tma_load_2d(base + L.w + (slot * NW + 0) * kRows * 128, &tmap0, st * kWordsPerStage, rb * kRows, fb, pol);
       if (NW == 2)
@@ -579,7 +582,7 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
           }
 #pragma unroll
           for (int m = 0; m < MTp; ++m) xcur[m] = xnext[m];
-          if (!p.sz_tma && !p.tiles0) {
+          if (!SZQ && !p.tiles0) {
             // scale / zero pairs (groups 2st, 2st+1) of the 64 rows: 4 bytes each
             const int row0 = rb * kRows;
 #pragma unroll
@@ -620,7 +623,7 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
 #pragma unroll
     for (int qq = 0; qq < 4; ++qq) x_off[qq] = L.x + frag_offset(MT, G, gc, t, qq);
     // scale/zero staging: 16-byte rows (quad slots) or 4-byte rows (ring slots)
-    const uint32_t rs = p.sz_tma ? 16u : 4u;
+    constexpr uint32_t rs = SZQ ? 16u : 4u;
     const uint32_t sz_mat = 2 * kRows * rs;  // bytes per (slot, mat)
     const uint32_t sz_lane = L.sz + pg * rs;
     float acc[NW][kTPW][4];
@@ -680,8 +683,8 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
           xs.x = ds[0];
           xs.y = ds[1];
         }
-        const uint32_t sz_slot = p.sz_tma ? (uint32_t)(pair * kSzQuadSlots + qs) : (uint32_t)slot;
-        const uint32_t sz_col = p.sz_tma ? (uint32_t)(st & 3) * 4u : 0u;
+        const uint32_t sz_slot = SZQ ? (uint32_t)(pair * kSzQuadSlots + qs) : (uint32_t)slot;
+        const uint32_t sz_col = SZQ ? (uint32_t)(st & 3) * 4u : 0u;
 #pragma unroll
         for (int mat = 0; mat < NW; ++mat) {
           const uint32_t sb = sz_lane + (sz_slot * NW + mat) * sz_mat + sz_col;
@@ -1035,7 +1038,7 @@ cudaLaunchAttribute pdl_attribute() {
 
 // Resident CTAs per SM for one kernel instantiation (cached per device).
 std::mutex g_occ_mutex;
-constexpr int kOccSlots = 20;
+constexpr int kOccSlots = 40;
 int g_occ[64][kOccSlots];
 
 int ctas_per_sm(const void* kern, int slot, int smem, int dev, int* out) {
@@ -1068,13 +1071,13 @@ int split_k_plan(int RB, int TS, int sm_count) {
   return 1;
 }
 
-template <int MT, int NW, int EPI>
+template <int MT, int NW, int EPI, bool SZQ>
 int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
              uint8_t* workspace, size_t ws_bytes, const DeviceInfo& dev, cudaStream_t stream) {
   constexpr Layout L = make_layout<MT, NW>();
   static_assert(L.total <= 227 * 1024, "shared-memory carve-up exceeds the per-CTA limit");
-  auto kern = w4a16_gemv_kernel<MT, NW, EPI>;
-  constexpr int slot = (MT == 1 ? 0 : MT == 2 ? 1 : MT == 4 ? 2 : 3) + 4 * EPI;  // < kOccSlots
+  auto kern = w4a16_gemv_kernel<MT, NW, EPI, SZQ>;
+  constexpr int slot = (MT == 1 ? 0 : MT == 2 ? 1 : MT == 4 ? 2 : 3) + 4 * EPI + (SZQ ? 20 : 0);  // < kOccSlots
   int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), slot, (int)L.total);
   if (rc) return rc;
   int occ = 0;
@@ -1135,11 +1138,19 @@ int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
 template <int NW, int EPI>
 int dispatch_mt(int MT, const CUtensorMap* maps, const Params& p, const __nv_bfloat16* x, uint8_t* ws,
                 size_t ws_bytes, const DeviceInfo& dev, cudaStream_t stream) {
+  if (p.sz_tma) {
+    switch (MT) {
+      case 1: return launch_t<1, NW, EPI, true>(maps, p, x, ws, ws_bytes, dev, stream);
+      case 2: return launch_t<2, NW, EPI, true>(maps, p, x, ws, ws_bytes, dev, stream);
+      case 4: return launch_t<4, NW, EPI, true>(maps, p, x, ws, ws_bytes, dev, stream);
+      default: return launch_t<8, NW, EPI, true>(maps, p, x, ws, ws_bytes, dev, stream);
+    }
+  }
   switch (MT) {
-    case 1: return launch_t<1, NW, EPI>(maps, p, x, ws, ws_bytes, dev, stream);
-    case 2: return launch_t<2, NW, EPI>(maps, p, x, ws, ws_bytes, dev, stream);
-    case 4: return launch_t<4, NW, EPI>(maps, p, x, ws, ws_bytes, dev, stream);
-    default: return launch_t<8, NW, EPI>(maps, p, x, ws, ws_bytes, dev, stream);
+    case 1: return launch_t<1, NW, EPI, false>(maps, p, x, ws, ws_bytes, dev, stream);
+    case 2: return launch_t<2, NW, EPI, false>(maps, p, x, ws, ws_bytes, dev, stream);
+    case 4: return launch_t<4, NW, EPI, false>(maps, p, x, ws, ws_bytes, dev, stream);
+    default: return launch_t<8, NW, EPI, false>(maps, p, x, ws, ws_bytes, dev, stream);
   }
 }
 
