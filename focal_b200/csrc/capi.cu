@@ -241,7 +241,7 @@ int focal_reset_device_status(void) {
   const int rc = current_device_info(&d);
   if (rc) return rc;
   *static_cast<volatile int*>(d.status_host) = 0;
-  return noalloc_clear_counters();
+  return noalloc_clear();
 }
 
 }  // extern "C"

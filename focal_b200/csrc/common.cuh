@@ -216,6 +216,15 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
   return v;
 }
 
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* addr, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* addr) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+  return v;
+}
+
 // ------------------------------------------------------------ cp.async (LDGSTS)
 // 16-byte copy global -> shared, bypassing L1 (.cg).
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {

@@ -30,8 +30,8 @@ struct DeviceInfo {
   int* status_host = nullptr;  // the same word, host view
 };
 
-// Zero the no-allocation GEMV scratch's counters on the current device (w4a16_gemv.cu).
-int noalloc_clear_counters();
+// Zero the no-allocation GEMV scratch on the current device (w4a16_gemv.cu).
+int noalloc_clear();
 
 // Attributes of the current device (cached per device ordinal).
 int current_device_info(DeviceInfo* out);

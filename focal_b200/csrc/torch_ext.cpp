@@ -38,7 +38,7 @@ cudaStream_t current_stream() {
 }
 
 // Device workspaces, one per (kind, device, stream), zeroed when allocated.
-// Their counters start at zero and every successful call leaves them at zero,
+// Their partial words start at zero and every successful call leaves them at zero,
 // and calls on one stream are ordered, so reuse is safe.  A workspace that is
 // outgrown stays allocated (a CUDA graph captured earlier may still use it).
 enum WsKind { kWsLinear = 0, kWsAttention = 1 };
@@ -48,7 +48,7 @@ std::vector<torch::Tensor> g_ws_retired;
 
 // A kernel that gave up a bounded device-side wait (a timed-out pipeline or
 // tensor-parallel peer) wrote a nonzero status word and may have left row-block
-// counters in a workspace nonzero.  Before every call that uses a workspace the
+// partial words in a workspace set.  Before every call that uses a workspace the
 // word is read (mapped host memory, no device sync); when it is set, every
 // cached workspace of the device is zeroed again on its own stream, the word is
 // cleared and the call raises, so the failure is reported once and later calls

@@ -140,31 +140,28 @@ __host__ __device__ constexpr uint32_t frag_offset(int MT, int G, int g, int t, 
 }
 
 // ------------------------------------------------- workspace layout
-// [row-block arrival counters: kMaxRowBlocks x 4 B][partials: 2P slots].  The
-// counters sit at the same place for every shape, start at zero and are left
-// at zero by every call (the range that finishes a row block clears its
-// counter), so one workspace serves calls of any shape in turn.
+// [partials: P slots of {fp32 bits, ready} words] (stream-K plan only).  Every
+// word starts at zero and is left at zero by every call (the row block's
+// finisher zeroes the words it read), so one workspace serves calls of any
+// shape in turn.
 constexpr int kMaxRowBlocks = 4096;  // N <= 262144
-constexpr size_t kCounterBytes = (size_t)kMaxRowBlocks * 4;
 struct WsLayout {
-  size_t counters, partials, total;
+  size_t partials, total;
 };
 
 __host__ __device__ inline size_t slot_floats(int MT, int NW) { return (size_t)NW * MT * kRows; }
 
 inline WsLayout ws_layout(int MT, int NW, int P) {
   WsLayout w;
-  w.counters = 0;
-  w.partials = kCounterBytes;
-  w.total = w.partials + 2 * (size_t)P * slot_floats(MT, NW) * 4;
+  w.partials = 0;
+  w.total = w.partials + (size_t)P * slot_floats(MT, NW) * 8;
   return w;
 }
 
 // ------------------------------------------------------------------ GEMV
 struct Params {
   const __nv_bfloat16* x;  // activations [M, K]
-  unsigned int* counters;  // per row block arrivals (zero between calls)
-  float* partials;         // [2P][NW][MT][64] split row-block partial sums
+  unsigned long long* partials;  // [P][NW][MT][64] {fp32 bits, ready} words: a range's share of its first row block
   const __half* scales0;
   const __half* zeros0;
   const __half* scales1;
@@ -606,7 +603,7 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     cp_async_wait<0>();  // no copy may land after this CTA exits
   } else {
     // ------------------------------------------------------------ consumers
-    griddep_wait();  // the previous call on this workspace has finished with its counters
+    griddep_wait();  // the previous call on this workspace has finished with its partial words
     if constexpr (is_tp(EPI)) tp_e = __ldcg(p.tp.state) + 1u;  // written by the previous call's last CTA
     const int tid = threadIdx.x;  // 0 .. kConsumerThreads-1
     const int g = lane >> 2, t = lane & 3;
@@ -838,64 +835,90 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
             finished(rb);
           }
         } else {
-          // publish this range's partial; the last of the row block's ranges finishes it
-          float* mine = p.partials + (2LL * vc + (rb == rb0 ? 0 : 1)) * slot_floats(MT, NW);
-          for (int o = ptid; o < nout; o += kPairThreads) {
-            const int tok = o / kRows, row = o - tok * kRows;
-#pragma unroll
-            for (int mat = 0; mat < NW; ++mat)
-              mine[(mat * MT + tok) * kRows + row] = red[(mat * MT + tok) * kRows + row];
-          }
-          // The barrier orders the pair's partial stores before thread 0's
-          // acquire-release increment, which publishes them at GPU scope; in
-          // the range that finishes the row block the same increment (acquire)
-          // and the barrier after it order the loads of every partial.
-          named_barrier(bar, kPairThreads);
+          // The row block is split over ranges c_first .. c_last.  Only c_first
+          // holds the row block at the end of its range (every later range
+          // starts inside it, so for them it is their first run, finished
+          // early): c_first is the finisher.  The others publish their share as
+          // 64-bit words {fp32 bits, 1} (the word carries its own ready flag, no
+          // fence or counter); the finisher adds its own share, then polls the
+          // others' words in range order (bounded), adds them (the same order
+          // and bits as a sum of all partials from c_first on) and zeroes the
+          // words it read, so the workspace is empty again for the next call.
           const int c_first = unit_owner(rb_lo, p.U, p.P), c_last = unit_owner(rb_hi - 1, p.U, p.P);
-          int* flag = reinterpret_cast<int*>(sm + L.flag) + pair;
-          if (ptid == 0) {
-            const unsigned int prev = atom_add_acq_rel_gpu(p.counters + rb, 1u);
-            *flag = (prev == (unsigned int)(c_last - c_first));
-          }
-          named_barrier(bar, kPairThreads);
-          if (*flag) {
-            // Partial slots: a range after c_first began inside this row block
-            // (slot 2c); c_first used slot 2c + 1 unless it began exactly at rb_lo.
-            const long long first_slot = 2LL * c_first + (unit_begin(c_first, p.U, p.P) == rb_lo ? 0 : 1);
-            if (ptid < kRows)
+          if (vc != c_first) {
+            unsigned long long* mine = p.partials + (size_t)vc * slot_floats(MT, NW);  // its first row block
+            for (int o = ptid; o < nout; o += kPairThreads) {
+              const int tok = o / kRows, row = o - tok * kRows;
+#pragma unroll
+              for (int mat = 0; mat < NW; ++mat) {
+                const int idx = (mat * MT + tok) * kRows + row;
+                st_relaxed_gpu_u64(mine + idx, (1ull << 32) | __float_as_uint(red[idx]));
+              }
+            }
+          } else if (ptid < kRows) {
             finish_block<MT, EPI, NW>(p, rb, ptid, tp_e, [&](float(&v)[MT][NW]) {
-              // every token's partials of kB ranges loaded together (one L2
-              // round trip per batch), added in range order (deterministic)
               constexpr int kB = MT * NW >= 8 ? 2 : MT * NW >= 4 ? 4 : kSumBatch;
 #pragma unroll
               for (int tok = 0; tok < MT; ++tok)
 #pragma unroll
-                for (int mat = 0; mat < NW; ++mat) v[tok][mat] = 0.f;
-              for (int cb = c_first; cb <= c_last; cb += kB) {
-                float part[kB][MT][NW];
+                for (int mat = 0; mat < NW; ++mat) v[tok][mat] = red[(mat * MT + tok) * kRows + ptid];
+              for (int cb = c_first + 1; cb <= c_last; cb += kB) {
+                // kB ranges' words requested together, re-polled until all carry the flag
+                unsigned long long w[kB][MT][NW];
 #pragma unroll
-                for (int e = 0; e < kB; ++e) {
-                  const int c = cb + e;
-                  const long long ps = c == c_first ? first_slot : 2LL * (c <= c_last ? c : cb);
-                  const float* src = p.partials + ps * slot_floats(MT, NW) + ptid;
+                for (int e = 0; e < kB; ++e)
 #pragma unroll
                   for (int tok = 0; tok < MT; ++tok)
 #pragma unroll
-                    for (int mat = 0; mat < NW; ++mat)
-                      part[e][tok][mat] =
-                          (c <= c_last && tok < p.M) ? __ldcg(src + (mat * MT + tok) * kRows) : 0.f;
+                    for (int mat = 0; mat < NW; ++mat) {
+                      const int c = cb + e;
+                      w[e][tok][mat] = (c <= c_last && tok < p.M)
+                                           ? ld_relaxed_gpu_u64(p.partials + (size_t)c * slot_floats(MT, NW) +
+                                                                (mat * MT + tok) * kRows + ptid)
+                                           : (1ull << 32);
+                    }
+                const long long t0 = clock64();
+                while (true) {
+                  bool ready = true;
+#pragma unroll
+                  for (int e = 0; e < kB; ++e)
+#pragma unroll
+                    for (int tok = 0; tok < MT; ++tok)
+#pragma unroll
+                      for (int mat = 0; mat < NW; ++mat) ready = ready && (w[e][tok][mat] >> 32) != 0ull;
+                  if (ready) break;
+                  if (clock64() - t0 > kWaitLimitCycles) {
+                    if (p.status) set_status(p.status, kDevWaitTimeout);  // this row block is garbage
+                    break;
+                  }
+#pragma unroll
+                  for (int e = 0; e < kB; ++e)
+#pragma unroll
+                    for (int tok = 0; tok < MT; ++tok)
+#pragma unroll
+                      for (int mat = 0; mat < NW; ++mat)
+                        if ((w[e][tok][mat] >> 32) == 0ull)
+                          w[e][tok][mat] = ld_relaxed_gpu_u64(p.partials + (size_t)(cb + e) * slot_floats(MT, NW) +
+                                                               (mat * MT + tok) * kRows + ptid);
                 }
 #pragma unroll
                 for (int e = 0; e < kB; ++e)
 #pragma unroll
                   for (int tok = 0; tok < MT; ++tok)
 #pragma unroll
-                    for (int mat = 0; mat < NW; ++mat) v[tok][mat] += part[e][tok][mat];
+                    for (int mat = 0; mat < NW; ++mat) {
+                      const int c = cb + e;
+                      if (c <= c_last && tok < p.M) {
+                        v[tok][mat] += __uint_as_float((unsigned int)w[e][tok][mat]);
+                        st_relaxed_gpu_u64(p.partials + (size_t)c * slot_floats(MT, NW) + (mat * MT + tok) * kRows +
+                                               ptid,
+                                           0ull);
+                      }
+                    }
               }
             });
-            if (ptid == 0) p.counters[rb] = 0u;
-            finished(rb);
           }
+          if (vc == c_first) finished(rb);
         }
         named_barrier(bar, kPairThreads);  // red and the flag are rewritten by the next run
 #ifdef FOCAL_TIMELINE
@@ -1113,8 +1136,7 @@ int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
   const WsLayout W = ws_layout(MT, NW, p.P);
   if (ws_bytes < W.total)
     return set_error(FOCAL_ERR_WORKSPACE, "workspace too small: need %zu bytes, got %zu", W.total, ws_bytes);
-  p.counters = reinterpret_cast<unsigned int*>(workspace + W.counters);
-  p.partials = reinterpret_cast<float*>(workspace + W.partials);
+  p.partials = reinterpret_cast<unsigned long long*>(workspace + W.partials);
   p.x = x;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
@@ -1349,10 +1371,10 @@ int noalloc_scratch(void** out) {
 
 }  // namespace gemv
 
-// Zero the no-allocation scratch's row-block counters on the current device if
-// they have been used there (after a device-side wait gave up they may be left
-// nonzero).  Allocates nothing.
-int noalloc_clear_counters() {
+// Zero the no-allocation scratch on the current device if it has been used
+// there (after a device-side wait gave up, partial words may be left set).
+// Allocates nothing.
+int noalloc_clear() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FOCAL_OK;
   void* ptr = nullptr;
@@ -1361,7 +1383,7 @@ int noalloc_clear_counters() {
     ptr = gemv::g_noalloc_ptr[dev];
   }
   if (!ptr) return FOCAL_OK;
-  return check_cuda(cudaMemset(ptr, 0, gemv::kCounterBytes), "cudaMemset(no-allocation scratch counters)");
+  return check_cuda(cudaMemset(ptr, 0, gemv::kNoAllocScratchBytes), "cudaMemset(no-allocation scratch)");
 }
 
 namespace gemv {

@@ -57,14 +57,13 @@ int focal_abi_version(void);
 int focal_w4a16_check_shape(int M, int K, int N);
 
 /* Bytes of device workspace the linear entry points below need for (M, K, N)
- * on the current device: 16 KB of arrival counters (one per 64 output rows,
- * N <= 262144) followed by the fp32 partial sums of row blocks that several
- * CTAs share.  0 if the shape is outside the contract.  The workspace needs
- * 256-byte alignment and must be zeroed once before its first call; every
- * call that returns FOCAL_OK leaves the counters at zero again, so one
- * workspace can serve calls of any shape (zero it again after a call that
- * failed on the device).  Calls that share a workspace must be ordered on one
- * stream. */
+ * on the current device: the partial sums of 64-row blocks whose K is split
+ * across CTAs, as 64-bit {fp32 bits, ready} words.  0 if the shape is outside
+ * the contract.  The workspace needs 256-byte alignment and must be zeroed once
+ * before its first call; every call that returns FOCAL_OK leaves every word at
+ * zero again, so one workspace can serve calls of any shape (zero it again
+ * after a call that failed on the device).  Calls that share a workspace must
+ * be ordered on one stream. */
 size_t focal_w4a16_workspace_size(int M, int K, int N);
 
 /* The linear layer.  Replaces launch_w4a16 / w4a16_gemv_kernel,
@@ -82,10 +81,10 @@ int focal_w4a16_gemv(const void* x, const int32_t* wq, const void* scales, const
  *    the check guards devices with many more SMs).
  *  - The first call on a device resolves the scratch's address
  *    (cudaGetSymbolAddress); make it before any stream capture.
- *  - The scratch's arrival counters start at zero when the library loads and
- *    every successful call leaves them at zero; after a call that failed on the
- *    device (focal_device_status nonzero) they may not be:
- *    focal_reset_device_status zeroes them again (a memset, no allocation).
+ *  - The scratch starts at zero when the library loads and every successful
+ *    call leaves it at zero; after a call that failed on the device
+ *    (focal_device_status nonzero) it may not be: focal_reset_device_status
+ *    zeroes it again (a memset, no allocation).
  *  - All calls on one device share the scratch, so calls that may overlap
  *    (different streams, or host threads without ordering) race; order them on
  *    one stream. */

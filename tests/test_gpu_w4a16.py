@@ -186,7 +186,7 @@ def test_capi_rejects_bad_shapes_and_pointers(cuda):
                             y.data_ptr(), 1, 512, 64, buf.data_ptr(), n, C.stream_ptr())
     assert rc == _lib.FOCAL_ERR_INVALID_VALUE and "aligned" in _lib.last_error()
     rc = L.focal_w4a16_gemv(x.data_ptr(), wq.data_ptr(), s.data_ptr(), z.data_ptr(),
-                            y.data_ptr(), 1, 512, 64, buf.data_ptr(), 1024, C.stream_ptr())
+                            y.data_ptr(), 1, 512, 64, buf.data_ptr(), 8, C.stream_ptr())
     assert rc == _lib.FOCAL_ERR_WORKSPACE
     status = __import__("ctypes").c_int(-1)
     assert L.focal_device_status(status) == 0 and status.value == 0

@@ -3,7 +3,7 @@ instead of a caller workspace, called through the C ABI.
 
 For callers that cannot allocate device memory where they call the layer.
 Collected last (file name) and independent of what ran before: the scratch's
-counters start at zero when the library loads and every call leaves them at
+words start at zero when the library loads and every call leaves them at
 zero.  Each case makes two calls in a row on different inputs and compares each
 with focal_w4a16_gemv (caller workspace) and the oracle.
 """
@@ -53,21 +53,21 @@ class _DevBytes:
         self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False), "version": 3}
 
 
-def test_noalloc_leaves_counters_zero(cuda):
-    """Every call leaves the scratch's row-block arrival counters (its first
-    16 KiB) at zero, including shapes whose row blocks are split across CTAs
-    and finished through those counters (K=8192, N=11008)."""
+def test_noalloc_leaves_scratch_zero(cuda):
+    """Every call leaves the scratch all zero again, including shapes whose row
+    blocks are split across CTAs and finished through partial words in the
+    scratch (K=8192, N=11008 and K=4096, N=28672 at M=8)."""
     import ctypes
 
-    for (M, K, N) in [(8, 8192, 11008), (1, 4096, 4096)]:
+    for (M, K, N) in [(8, 8192, 11008), (8, 4096, 28672), (1, 4096, 4096)]:
         x, wq, s, z = ow.baseline_case(M, K, N, seed=77)
         noalloc(C.to_dev_bf16(x, cuda), C.to_dev(wq, cuda), C.to_dev(s, cuda), C.to_dev(z, cuda))
     torch.cuda.synchronize()
     ptr, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
     _lib.call("focal_w4a16_noalloc_scratch", ctypes.byref(ptr), ctypes.byref(nbytes))
     assert nbytes.value == 8 << 20
-    counters = torch.as_tensor(_DevBytes(ptr.value, 16 << 10), device=cuda)
-    assert int(counters.count_nonzero()) == 0
+    scratch = torch.as_tensor(_DevBytes(ptr.value, nbytes.value), device=cuda)
+    assert int(scratch.count_nonzero()) == 0
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(cuda, monkeypatch):
