@@ -343,6 +343,49 @@ def weight_copies(case, n, device, seed):
     return out
 
 
+def refstyle_us(fn, device, warmup=30, iters=120, repeats=7):
+    """The reference benchmark's own timing (bench/bench_w4a16.py and
+    bench/bench_decode_bundle.py, time_cuda + summarize): `warmup` eager calls,
+    then per repeat `iters` eager calls back to back between two events, mean
+    per call; min / median / p90 / max over `repeats` (µs)."""
+    import torch
+
+    out = []
+    for _ in range(repeats):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        out.append(e0.elapsed_time(e1) * 1e3 / iters)
+    return summarize(out)
+
+
+def event_pair_floor_us(device, n=32, reps=3):
+    """Median time between two events around one trivial kernel (a 1-element
+    in-place multiply), queued behind a GPU sleep: the floor under any
+    single-call event measurement on this GPU (µs)."""
+    import torch
+
+    z = torch.zeros(1, device=device)
+    vals = []
+    for _ in range(reps):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        torch.cuda._sleep(20_000_000)
+        for a, b in evs:
+            a.record()
+            z.mul_(1)
+            b.record()
+        torch.cuda.synchronize(device)
+        vals += [a.elapsed_time(b) * 1e3 for a, b in evs]
+    return round(statistics.median(vals), 3)
+
+
 def per_shape_graph(device, peak, repeats=7):
     """Each sweep shape alone: L2-cold (enough weight copies, rotated, to exceed
     the 126 MB L2 several times over) and L2-warm (one weight set called back to
@@ -358,22 +401,10 @@ def per_shape_graph(device, peak, repeats=7):
         cases = weight_copies(F.baseline_case(M, K, N, seed=3000 + i, device=device), copies, device, 77 + i)
         cold, _ = graph_time_us([(lambda c=c: F.w4a16_linear(*c)) for c in cases], device, repeats)
         warm, _ = graph_time_us([lambda: F.w4a16_linear(*cases[0])] * 16, device, repeats)
-        # the reference's own timing (bench/bench_w4a16.py time_cuda): eager
-        # calls on one weight set, back to back between two events, mean per call
-        for _ in range(10):
-            F.w4a16_linear(*cases[0])
-        torch.cuda.synchronize(device)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(100):
-            F.w4a16_linear(*cases[0])
-        e1.record()
-        torch.cuda.synchronize(device)
-        refstyle = e0.elapsed_time(e1) * 1e3 / 100
+        refstyle = refstyle_us(lambda c=cases[0]: F.w4a16_linear(*c), device)
         rows.append({"M": M, "K": K, "N": N, "us": round(cold, 3), "GBps": round(nb / cold / 1e3, 1),
                      "frac": round(nb / cold / 1e3 / peak, 3), "us_warm": round(warm, 3),
-                     "us_refstyle": round(refstyle, 3)})
+                     "us_refstyle": refstyle["median"], "us_refstyle_stats": refstyle})
         del cases
     torch.cuda.empty_cache()
     return rows
@@ -404,9 +435,12 @@ def bundles(device, peak, repeats=7):
     calls = [(lambda cs=cs: [F.w4a16_linear(*c) for c in cs]) for cs in sets]
     cold, cold_s = graph_time_us(calls, device, repeats, min_calls=8)
     warm, warm_s = graph_time_us([calls[0]] * 8, device, repeats, min_calls=8)
+    # the reference's bundle timing: the seven eager calls on one weight set per
+    # iteration, 30 warm-up and 7 x 120 timed iterations
+    ref = refstyle_us(calls[0], device)
     out["decode_bundle"] = {
         "layers": [{"name": n, "M": M, "K": K, "N": N} for (n, M, K, N) in DECODE_BUNDLE],
-        "bytes": nb, "us_cold": summarize(cold_s), "us_warm": summarize(warm_s),
+        "bytes": nb, "us_cold": summarize(cold_s), "us_warm": summarize(warm_s), "us_refstyle": ref,
         "GBps_cold": round(nb / cold / 1e3, 1), "frac_cold": round(nb / cold / 1e3 / peak, 3)}
     del sets, calls
     mlp = []
@@ -609,6 +643,7 @@ def run_ours(args, rank, world, local):
     launch_us = ms_local * 1e3 / len(SWEEP)
     achieved = step_bytes / len(SWEEP) / (launch_us * 1e-6) / 1e9
     us_eager = per_launch_profile(cases)
+    floor_us = event_pair_floor_us(device)
     per_shape = None
     extra = {}
     if world == 1 and not args.no_secondary:
@@ -651,9 +686,12 @@ def run_ours(args, rank, world, local):
             "device_status": status.value,
             "per_shape": per_shape,
             "per_shape_note": "us: CUDA graph of L2-cold calls (rotating weight copies), median of 7; "
-                              "us_warm: same weights back to back in a graph; us_refstyle: 100 eager calls on "
-                              "one weight set back to back, mean (the reference benchmark's method); us_eager: "
-                              "one eager call between two events (includes launch processing)",
+                              "us_warm: same weights back to back in a graph; us_refstyle: the reference "
+                              "benchmark's method (30 warm-up eager calls on one weight set, then 120 back to "
+                              "back between two events, mean per call; median of 7 repeats, stats beside it); "
+                              "us_eager: one eager call between two events, queued behind a GPU sleep "
+                              "(event_pair_floor_us is the same measurement around a trivial kernel)",
+            "event_pair_floor_us": floor_us,
             **extra,
         }
         if tp is not None:
