@@ -547,7 +547,8 @@ def e2e_sweep(cases, steps, device):
 
 
 def attention_secondary(device, reps=20):
-    """GQA decode attention contract shapes (B, L), KV read cold from HBM."""
+    """GQA decode attention contract shapes (B, L), KV read cold from HBM: a
+    CUDA graph of calls on rotating KV copies, median of 7 timed replays."""
     import torch
 
     import focal_b200 as F
@@ -577,15 +578,19 @@ def attention_secondary(device, reps=20):
         graph.replay()
         torch.cuda.synchronize()
         n = max(1, reps // copies) if copies > 1 else reps
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(n):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (n * copies)
-        out.append({"B": B, "L": L, "us": round(us, 3), "GBps": round(nb / us / 1e3, 1)})
+        samples = []
+        for _ in range(7):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            samples.append(e0.elapsed_time(e1) * 1e3 / (n * copies))
+        us = statistics.median(samples)
+        out.append({"B": B, "L": L, "us": round(us, 3), "GBps": round(nb / us / 1e3, 1),
+                    "us_stats": summarize(samples)})
         del graph, kv
         torch.cuda.empty_cache()
     return out
