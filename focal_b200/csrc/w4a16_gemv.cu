@@ -81,9 +81,9 @@ constexpr int kSumBatch = 8;            // partial-sum ranges loaded together by
 constexpr int kMinUnitsPerRange = 4;    // below this, fewer ranges beat more split overhead
 // Scale/zero quad slots per sub-pipeline when they arrive by TMA: the slot of
 // quad k is refilled for quad k + 2, whose first unit is issued only after the
-// unit ring_of(NW) places earlier (a unit of quad k + 1, or of quad k when k is
-// a one-unit quad) was consumed, and consumption within a sub-pipeline is in
-// order.
+// unit p.depth <= ring_of(NW) places earlier (a unit of quad k + 1, or of quad
+// k when k is a one-unit quad) was consumed, and consumption within a
+// sub-pipeline is in order.
 constexpr int kSzQuadSlots = 2;
 constexpr int kSzQuadGroups = 8;        // groups per scale/zero TMA box (16 bytes of fp16)
 // bytes of scale/zero staging per weight matrix: quads by TMA (16-byte rows) or
@@ -171,6 +171,7 @@ struct Params {
   int M, K, N, G, TS, RB, P;
   int sz_tma;   // scales / zeros by TMA quads (needs G % 8 == 0 and 16-byte aligned bases)
   int csize;    // CTAs per cluster: > 1 splits each row block's K over a cluster (split_k_plan)
+  int depth;    // units a sub-pipeline keeps in flight ahead of its consumers (1 .. ring slots)
   const uint8_t* tiles0;  // unit-tiled weights (w4a16_tiles.h) instead of the maps, when set
   const uint8_t* tiles1;
   TpParams tp;  // tensor-parallel epilogues only
@@ -472,9 +473,9 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     // Weight boxes (and, when the unit opens a quad, the quad's scale / zero
     // boxes) of local unit j, on its slot's full barrier; the activation
     // record is written separately.
-    auto issue_unit = [&](int j, int rb, int st, bool opens_quad, int qs) {
+    auto issue_unit = [&](int j, int ri, int rb, int st, bool opens_quad, int qs) {
       TL(0, j);
-      const int slot = pp * R + j % R;
+      const int slot = pp * R + ri;  // ri = j % R
       const uint32_t fb = full_bar + 8 * slot;
       if (p.tiles0) {
         // unit-tiled: the weight image and the unit's scales / zeros are one
@@ -510,10 +511,10 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     // this sub-pipeline's weight (and quad) boxes
     {
       int rb = rb0, st = st0, qs = kSzQuadSlots - 1;
-      for (int j = 0; j < nu && j < R; ++j) {
+      for (int j = 0; j < nu && j < p.depth; ++j) {
         const bool oq = (j == 0) || ((st & 3) == 0);
         if (oq) qs = (qs + 1 == kSzQuadSlots) ? 0 : qs + 1;
-        if (lane == 0) issue_unit(j, rb, st, oq, qs);
+        if (lane == 0) issue_unit(j, j, rb, st, oq, qs);  // j < depth <= R
         if (++st == p.TS) {
           st = 0;
           ++rb;
@@ -555,21 +556,30 @@ __global__ void __maxnreg__(FOCAL_GEMV_MAXNREG)
     // slots as the consumers free them
     {
       int rb = rb0, st = st0, qs = kSzQuadSlots - 1;
+      int ri = 0;             // j % R
+      int rd = 0, phd = 0;    // (j - depth) % R and the parity of its ring pass
       uint4 xcur[MTp], xnext[MTp];
       if (nu > 0) load_x(xcur, st0);
       for (int j = 0; j < nu; ++j) {
         const bool oq = (j == 0) || ((st & 3) == 0);
         {
           if (oq) qs = (qs + 1 == kSzQuadSlots) ? 0 : qs + 1;
-          const int slot = pp * R + j % R;
+          const int slot = pp * R + ri;
           const uint32_t fb = full_bar + 8 * slot;
-          if (j >= R) {
-            if (!mbar_wait_bounded(empty_bar + 8 * slot, ((j / R) - 1) & 1)) {
+          if (j >= p.depth) {
+            // unit j - depth released: consumption is in order, so unit j - R,
+            // the last one in this slot, was released before it
+            if (!mbar_wait_bounded(empty_bar + 8 * (pp * R + rd), phd)) {
               ok = false;
               break;
             }
-            if (lane == 0) issue_unit(j, rb, st, oq, qs);
+            if (++rd == R) {
+              rd = 0;
+              phd ^= 1;
+            }
+            if (lane == 0) issue_unit(j, ri, rb, st, oq, qs);
           }
+          if (++ri == R) ri = 0;
           if (j + 1 < nu) load_x(xnext, st + 1 == p.TS ? 0 : st + 1);
           write_record(sm + L.x + slot * kRec, xcur);
           __syncwarp();
@@ -1124,10 +1134,26 @@ int launch_t(const CUtensorMap* maps, Params p, const __nv_bfloat16* x,
     const char* e = getenv("FOCAL_W4A16_ROWBLOCK");
     return !(e && atoi(e) == 0);
   }();
+  // Prefetch depth: the one-CTA-per-row-block plan runs on fewer SMs than the
+  // GPU has (N / 64 of them) and keeps the whole ring in flight; the plans that
+  // use every SM keep two units in flight per sub-pipeline, which measured
+  // faster than three (less HBM queueing ahead of each unit).
+  // FOCAL_W4A16_DEPTH_ROWBLOCK / FOCAL_W4A16_DEPTH override them (tuning).
+  static const int depth_rowblock = [] {
+    const char* e = getenv("FOCAL_W4A16_DEPTH_ROWBLOCK");
+    return e && atoi(e) > 0 ? atoi(e) : 1 << 20;
+  }();
+  static const int depth_other = [] {
+    const char* e = getenv("FOCAL_W4A16_DEPTH");
+    return e && atoi(e) > 0 ? atoi(e) : 2;
+  }();
+  constexpr int R = ring_of(NW);
+  p.depth = std::min(depth_other, R);
   if (p.csize > 1) {
     p.P = kPairs * p.csize * p.RB;  // CTA b: row block b / csize, K share b % csize
   } else if (rowblock && p.RB <= dev.sm_count && p.TS >= kPairs) {
     p.P = kPairs * p.RB;  // CTA b: row block b
+    p.depth = std::min(depth_rowblock, R);
   } else {
     p.P = (int)std::min<long long>((p.U + min_units - 1) / min_units, (long long)kPairs * dev.sm_count);
     p.P = std::max(p.P, 1);
