@@ -472,9 +472,12 @@ Plan make_plan(int B, int Hkv, int L, int sm_count) {
   const int bhn = B * Hkv;
   // Two CTAs per SM fit in shared memory; stay within one resident wave so
   // every CTA streams the same number of tiles at the same time.
-  // Long sequences: one CTA per SM (launched with the 6-stage ring), each
-  // split streaming at least four tiles, when that still covers 90 % of the
-  // SMs; otherwise two CTAs per SM, so more splits start at once.  FOCAL_ATTN_CTAS_PER_SM forces either (tuning).
+  // One CTA per SM (launched with the 6-stage ring) when the (sequence, KV
+  // head) pairs times their splits still cover 90 % of the SMs, or when the
+  // sequence is short (at most four tiles per split at one CTA per SM): fewer,
+  // longer splits with a deeper ring then beat more, shorter ones (B=1,
+  // L=4096: 9.1 -> 7.7 us; B=4, L=512: 5.7 -> 5.4 us).  Otherwise two CTAs per
+  // SM, so more splits start at once.  FOCAL_ATTN_CTAS_PER_SM forces either (tuning).
   static const int per_sm_env = [] {
     const char* e = getenv("FOCAL_ATTN_CTAS_PER_SM");
     return e && atoi(e) > 0 ? atoi(e) : 0;
@@ -486,7 +489,9 @@ Plan make_plan(int B, int Hkv, int L, int sm_count) {
   int per_sm = per_sm_env;
   if (per_sm == 0) {
     const int s1 = sm_count / bhn;
-    per_sm = (s1 >= 1 && pl.tiles / s1 >= 4 && 10 * bhn * s1 >= 9 * sm_count) ? 1 : 2;
+    const bool covers = s1 >= 1 && 10 * bhn * s1 >= 9 * sm_count;
+    const bool short_seq = s1 >= 1 && pl.tiles <= 4 * s1;
+    per_sm = (covers || short_seq) ? 1 : 2;
   }
   const int target = per_sm * sm_count;
   int s = target / bhn;
