@@ -86,18 +86,21 @@ def test_two_rank_group_over_nvlink():
     assert r.stdout.count("tp fused ok") == 2, r.stdout[-4000:]
 
 
-def test_missing_peer_times_out_with_status(cuda):
+@pytest.mark.parametrize("M,K,N", [(1, 1024, 256), (1, 256, 262144)])
+def test_missing_peer_times_out_with_status(cuda, M, K, N):
     """A two-rank group whose second buffer nobody ever writes (one GPU, one
-    kernel, a word that nothing sets): every bounded poll gives up after about
-    a second, the call's device status reads 2 (peer timeout), and the context
-    stays usable for later calls."""
+    kernel, a word that nothing sets): the bounded poll gives up after about a
+    second, the call's device status reads 2 (peer timeout), and the context
+    stays usable for later calls.  In the second shape every sub-pipeline
+    finishes about seven row blocks; once one poll of a CTA has given up its
+    later polls stop at once, so the call still takes about a second, not
+    seven."""
     import ctypes
     import time
 
     from focal_b200 import _lib
 
     L = _lib.lib()
-    M, K, N = 1, 1024, 256
     nbytes = int(L.focal_tp_buffer_size(2, M, N))
     bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=cuda) for _ in range(2)]
     comm = _lib.TpComm()
@@ -116,7 +119,7 @@ def test_missing_peer_times_out_with_status(cuda):
     waited = time.perf_counter() - t0
     status = ctypes.c_int(-1)
     assert L.focal_device_status(status) == 0 and status.value == 2, status.value
-    assert 0.3 < waited < 30, waited
+    assert 0.3 < waited < 4, waited
     assert L.focal_reset_device_status() == 0
     # the context still works: a plain call matches the oracle
     assert_close = ow.allclose_report(C.bf16_bits(C.gemv(x, wq, s, z)), ow.linear(*ow.baseline_case(M, K, N, seed=5)),
