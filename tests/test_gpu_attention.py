@@ -76,3 +76,28 @@ def test_capi_workspace_too_small(cuda):
     rc = _lib.lib().focal_gqa_decode_attn(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
                                           1, 32, 8, 4096, 128, 0.088, None, 0, C.stream_ptr())
     assert rc == _lib.FOCAL_ERR_WORKSPACE
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("B,L", [(1, 4096), (4, 700)])
+def test_head_sharded_attention(cuda, world, B, L):
+    """Tensor parallelism over KV heads (focal_b200.tp.heads_shard and
+    HeadParallelAttention), its ranks run in turn on one GPU: each rank's
+    shard of q and of the caches goes through the kernel, and the shards'
+    outputs joined in rank order (what gather_heads' all-gather does) match
+    the oracle on the full heads, and the unsharded kernel's output within
+    one bf16 step (the split plan depends on the number of heads)."""
+    from focal_b200 import tp
+
+    q, k, v = oa.random_case(B, 32, 8, L, 128, seed=40 + world)
+    dq, dk, dv = (C.to_dev_bf16(a, cuda) for a in (q, k, v))
+    parts = []
+    for rank in range(world):
+        ql, kl, vl = tp.heads_shard(dq, dk, dv, rank, world)
+        parts.append(tp.HeadParallelAttention()(ql, kl, vl))  # one-rank group: the shard's own output
+    o = torch.cat(parts, dim=1)
+    assert o.shape == (B, 32, 128)
+    check(o, q, k, v, f"heads world={world} B={B} L={L}")
+    full = focal_b200.gqa_decode_attention(dq, dk, dv)
+    diff = (o.float() - full.float()).abs()
+    assert float((diff / full.float().abs().clamp_min(1.0)).max()) <= 2 ** -7
